@@ -1,0 +1,128 @@
+/*
+ * ozaki_b200.h -- C ABI of the B200 (sm_100a) Ozaki-scheme GEMM library
+ * (liboz_b200.so).
+ *
+ * The library replaces the two device kernels of the reference
+ * implementation WhFanatic/Ozaki_triton (ozaki_triton.py) and the wrappers
+ * that launch them.  Every entry point takes plain device pointers, sizes,
+ * strides and a CUDA stream; it never allocates, frees or synchronises, and
+ * is re-entrant (no global state other than the last-error string, which is
+ * thread-local, and the device-side timeout flag described below).
+ *
+ * Status codes: 0 = OZ_OK; negative values are errors and oz_last_error()
+ * returns a message for the calling thread.  Argument errors are reported
+ * before any launch.
+ */
+#ifndef OZAKI_B200_H
+#define OZAKI_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types (matrix inputs, slices and outputs) */
+enum oz_dtype {
+  OZ_F64 = 0,
+  OZ_F32 = 1,
+  OZ_F16 = 2,
+  OZ_BF16 = 3,
+  OZ_I8 = 4
+};
+
+/* status codes */
+enum oz_status {
+  OZ_OK = 0,
+  OZ_ERR_INVALID = -1,     /* bad argument (shape, stride, alignment, range) */
+  OZ_ERR_UNSUPPORTED = -2, /* valid but unsupported combination */
+  OZ_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
+  OZ_ERR_TIMEOUT = -4      /* a device-side wait hit its bound (see oz_device_status) */
+};
+
+/* residual handling between split levels */
+enum oz_residual_mode {
+  OZ_RESIDUAL_COMPAT = 0, /* round the residual to fp32 after every level, as the
+                             reference's fp32 residual buffer does (bit-exact) */
+  OZ_RESIDUAL_EXACT = 1   /* keep the residual in the input precision (fp64) */
+};
+
+/* flags for oz_cross_gemm */
+#define OZ_GEMM_SKIP_TAIL 1u   /* drop slice pairs with i + j >= num_splits */
+
+/*
+ * Split alpha rule.  Replaces compute_split_bits (ozaki_triton.py:76-98):
+ * alpha = int((acc_bits - log2 n) / 2) with acc_bits 31 (int8 slices, int32
+ * accumulator) or 23 (float slices, fp32 accumulator), capped by the slice
+ * mantissa bits (fp32 23, fp16 10, bf16 7, int8 7).  Returns OZ_ERR_INVALID
+ * for n <= 0 or alpha < 1.
+ */
+int oz_compute_split_bits(int64_t n, int slice_dtype, int32_t *alpha_out);
+
+/*
+ * Bytes per slice row as the library lays slices out: k elements padded to a
+ * multiple of 128 bytes (the padding is written as zeros by oz_split).
+ */
+int64_t oz_slice_row_bytes(int64_t k, int slice_dtype);
+
+/*
+ * Split a batch of matrices into num_splits slices along K.
+ * Replaces split_matrix (ozaki_triton.py:214-256) and split_matrix_kernel
+ * (ozaki_triton.py:136-211).
+ *
+ *   in        : element (b, line, k) at in + b*stride_b + line*stride_line + k*stride_k
+ *               (element strides).  Lines are the rows of A, or the columns of B
+ *               (B is split through its transposed view, ozaki_triton.py:593).
+ *               Supported layouts: stride_k == 1, or stride_line == 1.
+ *   slices    : (batch, num_splits, lines, ld) of slice_dtype, ld = row pitch in
+ *               elements (oz_slice_row_bytes(k)/elem_size); k-contiguous.
+ *   scales    : (batch, num_splits, lines) fp32 powers of two.
+ *   residual_mode : OZ_RESIDUAL_COMPAT reproduces the reference bit for bit.
+ */
+int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+             int64_t stride_b, int64_t stride_line, int64_t stride_k,
+             int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
+             void *slices, int64_t ld, float *scales, void *stream);
+
+/*
+ * Fused cross-GEMM over all slice pairs.
+ * Replaces cross_gemm (ozaki_triton.py:455-498) and cross_gemm_kernel
+ * (ozaki_triton.py:305-452):
+ *   C[b] = out( sum_i sum_j od( f32( f32(A_i B_j^T) * sa_i ) * sb_j ) )
+ * summed i-major, j-minor; od = fp64 for an fp64 output, else fp32.
+ *
+ *   a_slices : (a_batches, s, m, ld) K-contiguous, ld as returned by oz_slice_row_bytes.
+ *   b_slices : (b_batches, s, n, ld) K-contiguous (B's slices stored transposed,
+ *              like B_slices_T at ozaki_triton.py:594).
+ *   a_scales : (a_batches, s, m) fp32; b_scales : (b_batches, s, n) fp32.
+ *   a_index / b_index : per output batch b, which A / B batch it uses (int32
+ *              device arrays of length batch; NULL means identity).  This is how
+ *              torch.matmul broadcasting is expressed without copying operands.
+ *   c        : (batch, m, n) of out_dtype, row pitch ldc elements.
+ *   flags    : OZ_GEMM_SKIP_TAIL or 0.
+ */
+int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_scales,
+                  const float *b_scales, int64_t batch, int64_t m, int64_t n, int64_t k,
+                  int64_t ld, int32_t num_splits, int slice_dtype, int out_dtype,
+                  const int32_t *a_index, const int32_t *b_index, int64_t a_batches,
+                  int64_t b_batches, void *c, int64_t ldc, uint32_t flags, void *stream);
+
+/*
+ * Device-side status: the kernels bound every spin-wait; when a bound is hit
+ * they record a code in a device flag and return early (their output is then
+ * undefined).  This call synchronises `stream`, returns OZ_OK or
+ * OZ_ERR_TIMEOUT, writes the recorded code (0 = none) to *code, and clears it.
+ */
+int oz_device_status(void *stream, int32_t *code);
+
+/* Message for the last error returned on the calling thread ("" if none). */
+const char *oz_last_error(void);
+
+/* Library version string. */
+const char *oz_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OZAKI_B200_H */

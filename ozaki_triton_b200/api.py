@@ -1,0 +1,302 @@
+"""Host side of the Ozaki-scheme GEMM: the reference's Python operator API.
+
+Same names, argument meaning and error behaviour as ``ozaki_triton.py`` of
+WhFanatic/Ozaki_triton (``compute_split_bits``, ``split_matrix``,
+``cross_gemm``, ``ozaki_matmul``); the device work goes through the C ABI of
+liboz_b200.so (hand-written sm_100a kernels).  Nothing here computes on the
+CPU and there is no Triton and no autotuner.
+
+Differences from the reference, all deliberate:
+* ``num_splits`` may be 1..8 (the reference stops at 4, ozaki_triton.py:563);
+* broadcast batch dimensions are not materialised: each distinct A and B
+  batch member is split once and the GEMM indexes them per output batch
+  (the reference copies the expanded operands, ozaki_triton.py:528-529);
+* slices are stored with their rows padded to a multiple of 128 bytes (the
+  tensor-memory-access tile width); ``split_matrix`` returns a view with the
+  reference's shape (B, s, M, K);
+* ``residual="exact"`` keeps the residual in fp64 between levels (the
+  reference rounds it to fp32, ozaki_triton.py:233); the default ``"auto"``
+  uses the reference's fp32 rounding for num_splits <= 4 (bit-exact slices)
+  and fp64 for num_splits > 4, where FP64 inputs need it to reach FP64
+  accuracy;
+* ``skip_tail=True`` drops the slice pairs with i + j >= num_splits.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+# ozaki_triton.py:36-41 -- slice dtype -> (mantissa bits, is integer)
+SLICE_DTYPE_INFO = {
+    torch.float32: (23, False),
+    torch.float16: (10, False),
+    torch.bfloat16: (7, False),
+    torch.int8: (7, True),
+}
+
+# ozaki_triton.py:43-49 -- accepted input dtypes
+INPUT_DTYPES = {torch.float64, torch.float32, torch.float16, torch.bfloat16}
+
+MAX_SPLITS = 8
+
+_OZ_DTYPE = {
+    torch.float64: _lib.OZ_F64,
+    torch.float32: _lib.OZ_F32,
+    torch.float16: _lib.OZ_F16,
+    torch.bfloat16: _lib.OZ_BF16,
+    torch.int8: _lib.OZ_I8,
+}
+
+
+def select_dot_accum_dtype(slice_dtype: torch.dtype) -> torch.dtype:
+    """Tensor-core accumulator: int32 for int8 slices, else fp32 (ozaki_triton.py:62-66)."""
+    return torch.int32 if slice_dtype == torch.int8 else torch.float32
+
+
+def select_out_accum_dtype(input_dtype: torch.dtype) -> torch.dtype:
+    """Outer accumulator: fp64 for fp64 inputs, else fp32 (ozaki_triton.py:69-73)."""
+    return torch.float64 if input_dtype == torch.float64 else torch.float32
+
+
+def compute_split_bits(n: int, slice_dtype: torch.dtype = torch.float16,
+                       dot_accum_dtype: torch.dtype = torch.float32) -> int:
+    """alpha = int((acc_bits - log2 n) / 2), capped by the slice bits (ozaki_triton.py:76-98).
+
+    Raises ValueError for an unknown accumulator or n <= 0 and AssertionError
+    when alpha < 1, like the reference.
+    """
+    if dot_accum_dtype == torch.int32:
+        acc_bits = 31
+    elif dot_accum_dtype == torch.float32:
+        acc_bits = 23
+    else:
+        raise ValueError(f"unsupported dot_accum_dtype: {dot_accum_dtype}")
+    slice_bits, _ = SLICE_DTYPE_INFO[slice_dtype]
+    alpha = int((acc_bits - math.log2(n)) / 2)
+    alpha = min(alpha, slice_bits)
+    assert alpha >= 1, f"n={n} too large to split safely (alpha={alpha})"
+    return alpha
+
+
+def slice_row_elems(k: int, slice_dtype: torch.dtype) -> int:
+    """Row pitch (elements) of the library's slice layout: k padded to 128 bytes."""
+    es = torch.empty((), dtype=slice_dtype).element_size()
+    return ((k * es + 127) // 128 * 128) // es if k > 0 else 0
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _residual_mode(residual: Optional[str], num_splits: int, input_dtype: torch.dtype) -> int:
+    if residual in (None, "auto"):
+        residual = "compat" if num_splits <= 4 else "exact"
+    if residual == "compat":
+        return _lib.OZ_RESIDUAL_COMPAT
+    if residual == "exact":
+        return _lib.OZ_RESIDUAL_EXACT
+    raise ValueError(f"unknown residual mode {residual!r}")
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("ozaki_triton_b200 computes on CUDA tensors only "
+                             f"(got a tensor on {t.device})")
+
+
+def _split_lines(x3: torch.Tensor, stride_line: int, stride_k: int, lines: int, k: int,
+                 num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int
+                 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Split the lines of a (batch, ., .) view; returns padded slices + scales."""
+    batch = x3.shape[0]
+    ld = slice_row_elems(k, slice_dtype)
+    slices = torch.empty((batch, num_splits, lines, ld), dtype=slice_dtype, device=x3.device)
+    scales = torch.empty((batch, num_splits, lines), dtype=torch.float32, device=x3.device)
+    if batch == 0 or lines == 0:
+        return slices, scales
+    lib = _lib.load()
+    _lib.check(lib.oz_split(
+        x3.data_ptr(), _OZ_DTYPE[x3.dtype], batch, lines, k,
+        x3.stride(0), stride_line, stride_k, num_splits, alpha, _OZ_DTYPE[slice_dtype], mode,
+        slices.data_ptr(), ld, scales.data_ptr(), _stream_ptr(x3.device)))
+    return slices, scales
+
+
+def split_matrix(A: torch.Tensor, num_splits: int, alpha: int, slice_dtype: torch.dtype,
+                 residual: Optional[str] = "compat") -> Tuple[torch.Tensor, torch.Tensor]:
+    """Split each row of A (B, M, K) into num_splits slices (ozaki_triton.py:214-256).
+
+    Any strides are accepted (e.g. the transposed view of B).  Returns
+    ``slices`` (B, num_splits, M, K) of ``slice_dtype`` -- a view of a buffer
+    whose rows are padded to 128 bytes -- and ``scales`` (B, num_splits, M)
+    fp32 powers of two.
+    """
+    assert A.dim() == 3
+    _check_cuda(A)
+    if A.dtype not in INPUT_DTYPES:
+        raise AssertionError(f"unsupported input dtype: {A.dtype}")
+    if slice_dtype not in SLICE_DTYPE_INFO:
+        raise AssertionError(f"unsupported slice dtype: {slice_dtype}")
+    B, M, K = A.shape
+    mode = _residual_mode(residual, num_splits, A.dtype)
+    slices, scales = _split_lines(A, A.stride(1), A.stride(2), M, K, num_splits, alpha,
+                                  slice_dtype, mode)
+    return slices[..., :K], scales
+
+
+def _as_library_slices(t: torch.Tensor, k: int) -> Tuple[torch.Tensor, int]:
+    """(batch, s, rows, k) K-contiguous slices in the padded library layout.
+
+    Returns the padded base tensor and its row pitch; copies only when the
+    given tensor is not already laid out that way.
+    """
+    batch, s, rows, kk = t.shape
+    assert kk == k
+    es = t.element_size()
+    ld = t.stride(2)
+    ok = (t.stride(3) == 1 and (ld * es) % 128 == 0 and ld >= k and t.stride(1) == rows * ld
+          and t.stride(0) == s * rows * ld and t.data_ptr() % 16 == 0)
+    if ok:
+        base = t.as_strided((batch, s, rows, ld), (s * rows * ld, rows * ld, ld, 1))
+        if ld == k or _pad_is_zero(base, k):
+            return base, ld
+    ld = slice_row_elems(k, t.dtype)
+    buf = torch.zeros((batch, s, rows, ld), dtype=t.dtype, device=t.device)
+    buf[..., :k] = t
+    return buf, ld
+
+
+def _pad_is_zero(base: torch.Tensor, k: int) -> bool:
+    # slices produced by split_matrix carry zero padding; anything else is
+    # re-laid out (checking costs one reduction, only for foreign tensors)
+    return bool((base[..., k:] == 0).all().item())
+
+
+def cross_gemm(A_slices: torch.Tensor, B_slices: torch.Tensor, A_scales: torch.Tensor,
+               B_scales: torch.Tensor, num_splits: int, output_dtype: torch.dtype,
+               skip_tail: bool = False, a_index: Optional[torch.Tensor] = None,
+               b_index: Optional[torch.Tensor] = None, batch: Optional[int] = None
+               ) -> torch.Tensor:
+    """Fused cross-GEMM over all slice pairs (ozaki_triton.py:455-498).
+
+    A_slices (BA, s, M, K); B_slices (BB, s, K, N) -- like the reference, the
+    transposed view of K-contiguous (BB, s, N, K) storage; scales fp32
+    (BA, s, M) / (BB, s, N).  Returns C (batch, M, N) in ``output_dtype``.
+    ``a_index`` / ``b_index`` (int32, CUDA) pick the A / B batch member of each
+    output batch (torch.matmul broadcasting); by default batch b uses member b.
+    """
+    assert A_slices.dim() == 4 and B_slices.dim() == 4
+    _check_cuda(A_slices, B_slices, A_scales, B_scales)
+    BA, s, M, K = A_slices.shape
+    BB, _, K2, N = B_slices.shape
+    assert K == K2
+    assert s == num_splits and B_slices.shape[1] == num_splits
+    slice_dtype = A_slices.dtype
+    assert B_slices.dtype == slice_dtype
+    if batch is None:
+        batch = BA if a_index is None else a_index.numel()
+    C = torch.empty((batch, M, N), dtype=output_dtype, device=A_slices.device)
+    if batch == 0 or M == 0 or N == 0:
+        return C
+    a_base, ld = _as_library_slices(A_slices, K)
+    b_base, ldb = _as_library_slices(B_slices.transpose(-1, -2), K)
+    assert ld == ldb
+    sa = A_scales.contiguous().float()
+    sb = B_scales.contiguous().float()
+    lib = _lib.load()
+    _lib.check(lib.oz_cross_gemm(
+        a_base.data_ptr(), b_base.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+        batch, M, N, K, ld, num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[output_dtype],
+        a_index.data_ptr() if a_index is not None else None,
+        b_index.data_ptr() if b_index is not None else None,
+        BA, BB, C.data_ptr(), N, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+        _stream_ptr(A_slices.device)))
+    return C
+
+
+def _batch_index(own: Tuple[int, ...], full: Tuple[int, ...], device) -> Optional[torch.Tensor]:
+    """Member of an operand with batch shape ``own`` used by each batch of ``full``."""
+    if tuple(own) == tuple(full):
+        return None
+    n_own = math.prod(own)
+    idx = torch.arange(n_own, dtype=torch.int32).reshape(own) if own else torch.zeros(
+        (), dtype=torch.int32)
+    idx = idx.expand(full).reshape(-1)
+    return idx.to(device, non_blocking=True)
+
+
+def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
+                 slice_dtype: torch.dtype = torch.float16, verbose: bool = False, *,
+                 skip_tail: bool = False, residual: Optional[str] = "auto") -> torch.Tensor:
+    """C = A @ B emulated with low-precision tensor-core slices (ozaki_triton.py:534-606).
+
+    A: (..., M, K), B: (..., K, N) of the same dtype (fp64/fp32/fp16/bf16),
+    batch dims broadcast like torch.matmul.  Returns (broadcast(...), M, N)
+    in the input dtype.
+    """
+    assert A.dtype == B.dtype, f"A/B dtype mismatch: {A.dtype} vs {B.dtype}"
+    assert A.dtype in INPUT_DTYPES, f"unsupported input dtype: {A.dtype}"
+    assert slice_dtype in SLICE_DTYPE_INFO, f"unsupported slice dtype: {slice_dtype}"
+    assert 1 <= num_splits <= MAX_SPLITS, \
+        f"num_splits must be in [1, {MAX_SPLITS}], got {num_splits}"
+    assert A.dim() >= 2 and B.dim() >= 2
+    M, K = A.shape[-2:]
+    K2, N = B.shape[-2:]
+    assert K == K2, f"contraction dim mismatch: A K={K}, B K={K2}"
+    _check_cuda(A, B)
+
+    input_dtype = A.dtype
+    dot_accum_dtype = select_dot_accum_dtype(slice_dtype)
+    a_batch, b_batch = tuple(A.shape[:-2]), tuple(B.shape[:-2])
+    batch_shape = tuple(torch.broadcast_shapes(a_batch, b_batch))
+    BN = math.prod(batch_shape)
+    out_shape = (*batch_shape, M, N)
+    if BN == 0:
+        return torch.empty(out_shape, dtype=input_dtype, device=A.device)
+
+    alpha = compute_split_bits(K, slice_dtype=slice_dtype, dot_accum_dtype=dot_accum_dtype)
+    if verbose:
+        print(f"[Ozaki] batch={batch_shape}, M={M}, K={K}, N={N}, "
+              f"input={input_dtype}, slice={slice_dtype}, "
+              f"dot_accum={dot_accum_dtype}, out_accum={select_out_accum_dtype(input_dtype)}, "
+              f"splits={num_splits}, alpha={alpha}")
+
+    mode = _residual_mode(residual, num_splits, input_dtype)
+    # split each distinct batch member once (no broadcast copies)
+    A3 = A.reshape(-1, M, K)
+    B3 = B.reshape(-1, K, N)
+    # B is split by columns: lines = N (stride 1 when B is row-major), k stride = N
+    b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), N, K, num_splits, alpha,
+                              slice_dtype, mode)
+    a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), M, K, num_splits, alpha,
+                              slice_dtype, mode)
+    a_idx = _batch_index(a_batch, batch_shape, A.device)
+    b_idx = _batch_index(b_batch, batch_shape, A.device)
+
+    C = torch.empty((BN, M, N), dtype=input_dtype, device=A.device)
+    if M and N:
+        lib = _lib.load()
+        ld = a_sl.shape[-1]
+        _lib.check(lib.oz_cross_gemm(
+            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(),
+            BN, M, N, K, ld, num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[input_dtype],
+            a_idx.data_ptr() if a_idx is not None else None,
+            b_idx.data_ptr() if b_idx is not None else None,
+            A3.shape[0], B3.shape[0], C.data_ptr(), N,
+            _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0, _stream_ptr(A.device)))
+    return C.view(out_shape)
+
+
+def device_status() -> int:
+    """Synchronise the current stream and return (and clear) the kernels'
+    timeout code (0 = none).  Raises OzakiError if a bound was hit."""
+    code = _lib.ctypes.c_int32(0)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.load().oz_device_status(st, _lib.ctypes.byref(code)))
+    return code.value
