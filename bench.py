@@ -1,0 +1,352 @@
+"""Benchmark of the Ozaki-scheme GEMM path on B200 (one JSON line on rank 0).
+
+Workload (BASELINE.json headline, config "C3"): FP64 -> INT8 slices,
+num_splits = 4, one GEMM with M = N = K = 8192, entries
+x = (U(0,1) - 0.5) * exp(N(0,1)) from seed 2 (synthetic, generated on the
+host).  One step = one ``ozaki_matmul``: split of A by rows, split of B by
+columns, fused cross-GEMM over the 16 slice pairs with the FP64 epilogue.
+
+* ``value``: emulated TFLOPS = 2*M*N*K / step time, inputs resident in HBM
+  (A and B are 512 MiB each, larger than L2, so no flush is needed).
+* ``e2e``: the same metric through the public ``ozaki_matmul`` call with the
+  operands in pinned host memory: host->device copies of A and B and the
+  device->host copy of C are inside the timed region.
+* ``roofline``: the cross-GEMM kernel, int8 tensor ops (pairs * 2MNK) per
+  launch over its CUDA-event duration, against 2x the measured dense bf16
+  peak (B200's dense int8 rate is twice its bf16 rate).
+* ``cpu_baseline``: the CPU restatement of the reference (oracle/) on a
+  bounded sample of the same workload, all host cores.
+
+Multi-GPU (torchrun, N > 1): A is sharded by M rows, B lives on rank 0,
+which splits it once and broadcasts the int8 slices + scales over NCCL
+(``ozaki_triton_b200.dist``); every rank computes its C rows.  Total work is
+fixed, so scaling is "strong".  ``--impl reference`` times the reference
+algorithm's CPU restatement on the host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N = K = 8192
+NUM_SPLITS = 4
+WORKLOAD = ("C3: FP64->INT8 Ozaki num_splits=4, single GEMM M=N=K=8192, "
+            "x=(U(0,1)-0.5)*exp(N(0,1)) seed 2")
+METRIC = "emulated TFLOPS (2MNK/t), FP64->INT8 s=4 8192^3"
+
+
+def make_inputs(seed: int = 2, m: int = M, n: int = N, k: int = K):
+    """Host fp64 operands of the headline law; draw order A's U, A's N, B's U, B's N."""
+    g = torch.Generator().manual_seed(seed)
+    ua = torch.rand(m, k, generator=g, dtype=torch.float64)
+    na = torch.randn(m, k, generator=g, dtype=torch.float64)
+    ub = torch.rand(k, n, generator=g, dtype=torch.float64)
+    nb = torch.randn(k, n, generator=g, dtype=torch.float64)
+    return (ua - 0.5) * torch.exp(na), (ub - 0.5) * torch.exp(nb)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per cross-GEMM launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            return json.load(fh)
+    return None
+
+
+def cpu_baseline_sample(seconds_budget: float = 20.0):
+    """The oracle (CPU restatement of the reference) on row/column samples."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ms = ns = 256
+    a, b = make_inputs(seed=2, m=ms, n=ns, k=K)
+    a, b = a.numpy(), b.numpy()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.ozaki_matmul(a, b, NUM_SPLITS, "int8", "fp64")
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > seconds_budget or len(times) >= 5:
+            break
+    t = statistics.median(times)
+    return {"value": 2.0 * ms * ns * K / t / 1e12, "unit": "TFLOPS", "cores": threads,
+            "kind": "port",
+            "sample": f"{ms}x{ns} block of C with full K={K} (A rows x B columns of the "
+                      f"workload law), numpy oracle, median of {len(times)}"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ms = ns = 256
+    a, b = make_inputs(seed=2, m=ms, n=ns, k=K)
+    a, b = a.numpy(), b.numpy()
+    for _ in range(args.warmup):
+        oracle.ozaki_matmul(a, b, NUM_SPLITS, "int8", "fp64")
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.ozaki_matmul(a, b, NUM_SPLITS, "int8", "fp64")
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    v = 2.0 * ms * ns * K / dt / 1e12
+    line = {"metric": METRIC, "value": v, "unit": "TFLOPS", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sample": f"{ms}x{ns}x{K} per step"},
+            "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                             "sample": f"{ms}x{ns} block of C, full K={K}, per step"},
+            "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "the reference is Python/Triton and cannot run on the GPU box; this arm "
+                    "times its CPU restatement (oracle/) with all host threads"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-dgemm", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="timed steps only (no e2e, DGEMM or CPU legs): the ncu command line")
+    args = ap.parse_args()
+    if args.profile:
+        args.no_e2e = args.no_cpu_baseline = args.no_dgemm = True
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        from ozaki_triton_b200 import dist_bench
+        dist_bench.main(args)
+        return
+    run_single(args)
+
+
+def run_single(args):
+    import ozaki_triton_b200 as oz
+    from ozaki_triton_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    a_h, b_h = make_inputs()
+    a = a_h.to(dev)
+    b = b_h.to(dev)
+    stream = torch.cuda.current_stream()
+
+    # per-step device timing of the dominant kernel: events around the GEMM
+    gemm_events = []
+
+    def step(record: bool):
+        alpha = oz.compute_split_bits(K, torch.int8, torch.int32)
+        from ozaki_triton_b200.api import _split_lines, _OZ_DTYPE
+        b_sl, b_sc = _split_lines(b.reshape(1, K, N), 1, N, N, K, NUM_SPLITS, alpha,
+                                  torch.int8, _lib.OZ_RESIDUAL_COMPAT)
+        a_sl, a_sc = _split_lines(a.reshape(1, M, K), K, 1, M, K, NUM_SPLITS, alpha,
+                                  torch.int8, _lib.OZ_RESIDUAL_COMPAT)
+        c = torch.empty((M, N), dtype=torch.float64, device=dev)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        _lib.check(_lib.load().oz_cross_gemm(
+            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), 1, M, N, K,
+            a_sl.shape[-1], NUM_SPLITS, _OZ_DTYPE[torch.int8], _OZ_DTYPE[torch.float64],
+            None, None, 1, 1, c.data_ptr(), N, 0, stream.cuda_stream))
+        if record:
+            e1.record(stream)
+            gemm_events.append((e0, e1))
+        return c
+
+    # the public call, checked once against the step above
+    for _ in range(args.warmup):
+        step(False)
+    c_api = oz.ozaki_matmul(a, b, num_splits=NUM_SPLITS, slice_dtype=torch.int8)
+    c_step = step(False)
+    torch.cuda.synchronize()
+    assert torch.equal(c_api, c_step)
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
+    flops = 2.0 * M * N * K
+    value = flops / (ms * 1e-3) / 1e12
+    pairs = NUM_SPLITS * NUM_SPLITS
+    bf16_peak, hbm_peak, peak_src = peaks()
+    int8_peak = 2.0 * bf16_peak
+    achieved = pairs * flops / (gemm_ms * 1e-3) / 1e12
+
+    # accuracy and speed next to cuBLAS DGEMM
+    rel_err = dgemm_tflops = None
+    if not args.no_dgemm:
+        ref = a @ b
+        c = step(False)
+        rel_err = ((c - ref).norm() / ref.norm()).item()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        for _ in range(2):
+            torch.matmul(a, b)
+        t0.record(stream)
+        for _ in range(3):
+            torch.matmul(a, b)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        dgemm_tflops = flops / (t0.elapsed_time(t1) / 3 * 1e-3) / 1e12
+        del ref, c
+
+    # end to end through the public call with host operands
+    e2e = None
+    if not args.no_e2e:
+        a_pin = a_h.pin_memory()
+        b_pin = b_h.pin_memory()
+        c_pin = torch.empty((M, N), dtype=torch.float64).pin_memory()
+
+        def e2e_step():
+            ad = a_pin.to(dev, non_blocking=True)
+            bd = b_pin.to(dev, non_blocking=True)
+            cd = oz.ozaki_matmul(ad, bd, num_splits=NUM_SPLITS, slice_dtype=torch.int8)
+            c_pin.copy_(cd, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(2, min(args.steps, 5))
+        s0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = s0.elapsed_time(s1) / e2e_steps
+        e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": 2 * M * K * 8,
+               "d2h_bytes_per_step": M * N * 8}
+
+    traffic = committed_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "num_splits": NUM_SPLITS,
+                   "slice_dtype": "int8", "input_dtype": "fp64", "residual": "compat",
+                   "l2": "no flush: A and B are 512 MiB each, larger than the 126 MB L2",
+                   "parallelism": "1 GPU"},
+        "roofline": {"bound": "tensor", "kernel": "cross_gemm_kernel<i8,f64,128>",
+                     "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / int8_peak,
+                     "peak_source": f"2x {peak_src} dense bf16 ({bf16_peak} TF/s, "
+                                    "MEASURED_PEAKS.json); B200 dense int8 = 2x bf16",
+                     "gemm_ms": gemm_ms,
+                     "traffic": traffic.get("cross_gemm_bytes_per_launch") if traffic else None},
+        "rel_err_vs_dgemm": rel_err,
+        "cublas_dgemm_tflops": dgemm_tflops,
+        "clocks": clk.summary(),
+        "gpu_launches": 3 * args.steps,
+        "e2e": e2e,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

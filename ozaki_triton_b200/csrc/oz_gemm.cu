@@ -271,8 +271,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int js = p.skip_tail ? s - i : s;
         const int buf = pass % nbuf;
         const uint32_t use = pass / nbuf;
-        if (!(ok = mbar_wait_bounded(&acc_full[buf], use & 1, abort_flag, DEV_TIMEOUT_EPILOGUE)))
-          break;
+        // every lane waits, then the warp agrees (tcgen05.ld needs a converged warp)
+        ok = mbar_wait_bounded(&acc_full[buf], use & 1, abort_flag, DEV_TIMEOUT_EPILOGUE);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
         tc_fence_after();
         const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         for (int j = 0; j < js; ++j) {

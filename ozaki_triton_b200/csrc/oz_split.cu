@@ -381,7 +381,7 @@ int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines,
   constexpr int VEC = 16 / (int)sizeof(TIn);
   // 16-byte vector loads need 16-byte aligned rows
   const bool vec_ok = ((uintptr_t)in % 16 == 0) && (sl * (int64_t)sizeof(TIn)) % 16 == 0 &&
-                      (sb * (int64_t)sizeof(TIn)) % 16 == 0 && K % VEC == 0 &&
+                      (sb * (int64_t)sizeof(TIn)) % 16 == 0 && K % VEC == 0 && ld % VEC == 0 &&
                       ((int64_t)ld * (int64_t)sizeof(ST)) % 16 == 0;
   *done = false;
   if (!vec_ok) return OZ_OK;

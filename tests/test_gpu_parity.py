@@ -1,0 +1,297 @@
+"""Parity of the CUDA path (through the C ABI) with the reference's golden
+vectors and with the CPU oracle.  Needs a B200."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import ozaki_triton_b200 as oz
+from golden_cases import matmul_cases, np_input, same_bits, split_cases
+
+pytestmark = pytest.mark.gpu
+
+TDT = {"fp64": torch.float64, "fp32": torch.float32, "fp16": torch.float16,
+       "bf16": torch.bfloat16, "int8": torch.int8}
+KINDS = {v: k for k, v in TDT.items()}
+DEV = "cuda"
+
+
+def to_dev(x_np, kind):
+    return torch.from_numpy(np.ascontiguousarray(x_np)).to(TDT[kind]).to(DEV)
+
+
+def host(t):
+    if t.dtype == torch.bfloat16 or t.dtype == torch.float16:
+        return t.float().cpu().numpy()
+    return t.cpu().numpy()
+
+
+def check_split(x_dev, lines_np, s, alpha, sk, ik, residual="compat"):
+    """Run split_matrix on x_dev (B, L, K) (any strides) and compare with the oracle."""
+    sl, sc = oz.split_matrix(x_dev, s, alpha, TDT[sk], residual=residual)
+    rsl, rsc = oracle.split_lines(lines_np, s, alpha, sk, ik, residual=residual)
+    torch.cuda.synchronize()
+    assert oz.device_status() == 0
+    assert same_bits(host(sc), rsc)
+    got = host(sl)
+    want = rsl if sk == "int8" else rsl.astype(np.float32)
+    assert same_bits(got, want)
+
+
+# ------------------------------------------------------------------ golden
+SPLITS = split_cases()
+
+
+@pytest.mark.parametrize("case", SPLITS, ids=[c["name"] for c in SPLITS])
+def test_split_matches_reference_golden(case):
+    ik, sk = case["input_kind"], case["slice_kind"]
+    x = to_dev(case["x"], ik)
+    view = x if case["layout"] == "rows" else x.transpose(-1, -2)
+    sl, sc = oz.split_matrix(view, case["s"], case["alpha"], TDT[sk])
+    torch.cuda.synchronize()
+    assert same_bits(host(sc), case["scales"])
+    got = host(sl)
+    want = case["slices"]
+    assert same_bits(got if sk == "int8" else got.astype(np.float64),
+                     want if sk == "int8" else want.astype(np.float64))
+
+
+MATMULS = matmul_cases()
+
+
+@pytest.mark.parametrize("case", MATMULS, ids=[c["name"] for c in MATMULS])
+def test_matmul_matches_reference_golden(case):
+    ik, sk = case["input_kind"], case["slice_kind"]
+    a, b = to_dev(case["a"], ik), to_dev(case["b"], ik)
+    c = oz.ozaki_matmul(a, b, num_splits=case["s"], slice_dtype=TDT[sk])
+    got = host(c).astype(np.float64)
+    ref = case["c"].astype(np.float64)
+    assert got.shape == ref.shape
+    if sk == "int8":
+        # int8 slice products are exact in int32 and the epilogue follows the
+        # reference's order: bit-exact
+        assert same_bits(got, ref)
+    else:
+        err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+        assert err < (2e-3 if ik in ("fp16", "bf16") else 1e-6), err
+
+
+# ------------------------------------------------------------------ split vs oracle
+def rand_lines(rng, shape, kind):
+    x = rng.standard_normal(shape) * 10.0 ** rng.uniform(-2, 2, shape[:-1] + (1,))
+    if kind in ("fp16", "bf16"):
+        x = np.clip(x, -6e4, 6e4)
+    return x
+
+
+COMBOS = [(ik, sk) for ik in ("fp64", "fp32", "fp16", "bf16") for sk in ("int8", "fp16", "bf16", "fp32")]
+
+
+@pytest.mark.parametrize("ik,sk", COMBOS)
+@pytest.mark.parametrize("K", [1, 37, 256, 1000, 4096])
+def test_split_rows_all_dtypes(ik, sk, K):
+    rng = np.random.default_rng(K * 31 + len(ik) * 7 + len(sk))
+    x = rand_lines(rng, (2, 19, K), ik)
+    xd = to_dev(x, ik)
+    lines = host(xd).astype(np.float64 if ik == "fp64" else np.float32)
+    s = 3
+    alpha = oz.compute_split_bits(max(K, 1), TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    check_split(xd, lines, s, alpha, sk, ik)
+
+
+@pytest.mark.parametrize("ik,sk", [("fp64", "int8"), ("fp32", "fp16"), ("fp16", "int8"),
+                                   ("bf16", "bf16"), ("fp64", "fp16"), ("fp32", "int8")])
+@pytest.mark.parametrize("K", [5, 128, 1000, 3000, 8192, 16384])
+def test_split_cols_all_sizes(ik, sk, K):
+    """Columns of a row-major (K, N) matrix: the cluster kernel."""
+    rng = np.random.default_rng(K + 5)
+    N = 45
+    b = rand_lines(rng, (1, N, K), ik)              # lines first, then store transposed
+    bd = to_dev(np.swapaxes(b, -1, -2), ik)         # (1, K, N) row-major
+    lines = host(bd).astype(np.float64 if ik == "fp64" else np.float32)
+    lines = np.swapaxes(lines, -1, -2)
+    alpha = oz.compute_split_bits(K, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    check_split(bd.transpose(-1, -2), lines, 4, alpha, sk, ik)
+
+
+@pytest.mark.parametrize("residual", ["compat", "exact"])
+@pytest.mark.parametrize("s", [1, 2, 5, 8])
+def test_split_levels_and_residual_modes(residual, s):
+    rng = np.random.default_rng(s)
+    x = (rng.uniform(0, 1, (1, 33, 700)) - 0.5) * np.exp(4 * rng.standard_normal((1, 33, 700)))
+    xd = to_dev(x, "fp64")
+    check_split(xd, x, s, 7, "int8", "fp64", residual=residual)
+    check_split(xd.transpose(-1, -2).contiguous().transpose(-1, -2), x, s, 7, "int8", "fp64",
+                residual=residual)
+
+
+def test_split_generic_strides():
+    """Neither the split axis nor the lines contiguous: the generic kernel."""
+    rng = np.random.default_rng(3)
+    big = rng.standard_normal((2, 40, 3, 90))
+    xd = to_dev(big, "fp64")[:, :, 1, :]            # (2, 40, 90), strides (10800, 270, 1)
+    check_split(xd, big[:, :, 1, :], 4, 7, "int8", "fp64")
+    xt = to_dev(big, "fp64").permute(0, 3, 2, 1)[:, :, 1, :]   # (2, 90, 40), both strided
+    check_split(xt, np.ascontiguousarray(big.transpose(0, 3, 2, 1)[:, :, 1, :]), 3, 7, "fp16",
+                "fp64")
+
+
+def test_split_unaligned_row_pitch():
+    """K not a multiple of the 16-byte vector: vector path refused, generic path used."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((1, 10, 77))
+    xd = to_dev(x, "fp32")
+    check_split(xd, x.astype(np.float32), 2, 6, "fp16", "fp32")
+
+
+def test_split_edge_rows():
+    K = 512
+    rows = np.zeros((6, K))
+    rows[1, :4] = [1.0, 0.5, -1.0, 0.3]
+    rows[2, :] = 1e-300
+    rows[3, ::3] = -2.0 ** 40
+    rows[4, :] = np.ldexp(1.0 + np.arange(K) % 7 * 2.0 ** -23, np.arange(K) % 50 - 25)
+    rows[5, :] = (np.arange(K) - 256 + 0.5) / 2.0 ** 7
+    xd = to_dev(rows[None], "fp64")
+    check_split(xd, rows[None], 4, 7, "int8", "fp64")
+    check_split(xd.transpose(-1, -2).contiguous().transpose(-1, -2), rows[None], 4, 7, "int8",
+                "fp64")
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("s", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("shape", [(128, 128, 128), (200, 72, 300), (1, 1, 1), (257, 383, 1000)])
+def test_int8_pair_products_exact(s, shape):
+    """Each int8 pair product is exact in int32: with unit scales C is the
+    exact integer sum over all pairs."""
+    M, N, K = shape
+    g = torch.Generator().manual_seed(M + N + K + s)
+    a = torch.randint(-128, 128, (1, s, M, K), generator=g, dtype=torch.int8)
+    b = torch.randint(-128, 128, (1, s, N, K), generator=g, dtype=torch.int8)
+    sa = torch.ones((1, s, M))
+    sb = torch.ones((1, s, N))
+    c = oz.cross_gemm(a.to(DEV), b.to(DEV).transpose(-1, -2), sa.to(DEV), sb.to(DEV), s,
+                      torch.float64)
+    want = (a.sum(1).long()[0] @ b.sum(1).long()[0].T).double()
+    assert torch.equal(c[0].cpu(), want)
+
+
+@pytest.mark.parametrize("sk", ["int8", "fp16", "bf16", "fp32"])
+@pytest.mark.parametrize("out", ["fp64", "fp32", "fp16", "bf16"])
+def test_cross_gemm_dtypes_vs_oracle(sk, out):
+    rng = np.random.default_rng(11)
+    s, M, N, K = 3, 150, 140, 333
+    a = rng.standard_normal((2, M, K)); b = rng.standard_normal((2, N, K))
+    alpha = oz.compute_split_bits(K, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    asl, asc = oracle.split_lines(a, s, alpha, sk, "fp64")
+    bsl, bsc = oracle.split_lines(b, s, alpha, sk, "fp64")
+    want = oracle.cross_gemm(asl, bsl, asc, bsc, sk, out).astype(np.float64)
+    def dev_slices(x):
+        t = torch.from_numpy(x.astype(np.float32) if sk != "int8" else x)
+        return t.to(TDT[sk]).to(DEV)
+    c = oz.cross_gemm(dev_slices(asl), dev_slices(bsl).transpose(-1, -2),
+                      torch.from_numpy(asc).to(DEV), torch.from_numpy(bsc).to(DEV), s, TDT[out])
+    got = host(c).astype(np.float64)
+    if sk == "int8" and out in ("fp64", "fp32"):
+        assert same_bits(got, want)
+    else:
+        tol = {"fp64": 1e-6, "fp32": 1e-6, "fp16": 2e-3, "bf16": 1e-2}[out]
+        if sk == "fp32":
+            tol = max(tol, 2e-3)   # TF32 tensor-core inputs keep 10 mantissa bits
+        err = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert err < tol, err
+
+
+@pytest.mark.parametrize("ik,sk,s", [("fp64", "int8", 4), ("fp32", "int8", 3), ("fp64", "int8", 6),
+                                     ("fp64", "fp16", 3), ("fp32", "fp16", 2), ("fp64", "bf16", 3),
+                                     ("fp16", "fp32", 1), ("bf16", "fp16", 2)])
+@pytest.mark.parametrize("shape", [(300, 200, 520), (129, 64, 8192), (1024, 1024, 1024)])
+def test_matmul_vs_oracle(ik, sk, s, shape):
+    M, N, K = shape
+    rng = np.random.default_rng(M * 3 + N + s)
+    a = (rng.uniform(0, 1, (M, K)) - 0.5) * np.exp(rng.standard_normal((M, K)))
+    b = (rng.uniform(0, 1, (K, N)) - 0.5) * np.exp(rng.standard_normal((K, N)))
+    ad, bd = to_dev(a, ik), to_dev(b, ik)
+    a_np = host(ad).astype(np.float64 if ik == "fp64" else np.float32)
+    b_np = host(bd).astype(np.float64 if ik == "fp64" else np.float32)
+    c = oz.ozaki_matmul(ad, bd, num_splits=s, slice_dtype=TDT[sk])
+    residual = "compat" if s <= 4 else "exact"
+    want = oracle.ozaki_matmul(a_np, b_np, s, sk, ik, residual=residual).astype(np.float64)
+    got = host(c).astype(np.float64)
+    if sk == "int8":
+        assert same_bits(got, want)
+    else:
+        # the tensor cores accumulate each pair product over K in fp32 (as the
+        # reference's tl.dot does); the oracle rounds the exact product once
+        err = np.linalg.norm(got - want) / np.linalg.norm(want)
+        tol = 2e-3 if ik in ("fp16", "bf16") else max(1e-6, 2.5e-7 * np.sqrt(K))
+        assert err < tol, err
+
+
+def test_broadcast_batch_semantics():
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((4, 1, 3, 40, 64))
+    b = rng.standard_normal((2, 1, 64, 24))
+    ad, bd = to_dev(a, "fp64"), to_dev(b, "fp64")
+    c = oz.ozaki_matmul(ad, bd, num_splits=4, slice_dtype=torch.int8)
+    assert c.shape == torch.matmul(ad, bd).shape
+    want = oracle.ozaki_matmul(a, b, 4, "int8", "fp64")
+    assert same_bits(host(c), want)
+
+
+def test_skip_tail_matches_oracle():
+    rng = np.random.default_rng(6)
+    a = rng.standard_normal((96, 256)); b = rng.standard_normal((256, 80))
+    c = oz.ozaki_matmul(to_dev(a, "fp64"), to_dev(b, "fp64"), num_splits=4,
+                        slice_dtype=torch.int8, skip_tail=True)
+    want = oracle.ozaki_matmul(a, b, 4, "int8", "fp64", skip_tail=True)
+    assert same_bits(host(c), want)
+
+
+def test_error_paths():
+    a = torch.randn(8, 16, device=DEV, dtype=torch.float64)
+    b = torch.randn(16, 4, device=DEV, dtype=torch.float64)
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a, b.float())
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a.to(torch.int32), b.to(torch.int32))
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a, b, num_splits=9)
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a, b, num_splits=0)
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a, torch.randn(15, 4, device=DEV, dtype=torch.float64))
+    with pytest.raises(AssertionError):
+        oz.ozaki_matmul(a, b, slice_dtype=torch.float64)
+    with pytest.raises(ValueError):   # K == 0: log2(0), like the reference
+        oz.ozaki_matmul(torch.zeros(3, 0, device=DEV), torch.zeros(0, 2, device=DEV))
+    with pytest.raises(AssertionError):   # alpha < 1
+        oz.ozaki_matmul(torch.zeros(1, 2 ** 22, device=DEV), torch.zeros(2 ** 22, 1, device=DEV),
+                        num_splits=1, slice_dtype=torch.float16)
+    # empty batch and empty M / N
+    assert oz.ozaki_matmul(torch.zeros(0, 3, 4, device=DEV), torch.zeros(4, 2, device=DEV)).shape == (0, 3, 2)
+    assert oz.ozaki_matmul(torch.zeros(0, 4, device=DEV), torch.zeros(4, 2, device=DEV)).shape == (0, 2)
+    assert oz.device_status() == 0
+
+
+def test_headline_size_properties():
+    """8192^3 fp64 -> int8, s=4 at full size: exact against the oracle on a
+    sample of rows x columns (the split is per line, so a sub-block of C is
+    reproduced exactly from its A rows and B columns), and accuracy against
+    an fp64 matmul."""
+    M = N = K = 8192
+    g = torch.Generator().manual_seed(2)
+    a = (torch.rand(M, K, generator=g, dtype=torch.float64) - 0.5) * torch.exp(
+        torch.randn(M, K, generator=g, dtype=torch.float64))
+    b = (torch.rand(K, N, generator=g, dtype=torch.float64) - 0.5) * torch.exp(
+        torch.randn(K, N, generator=g, dtype=torch.float64))
+    ad, bd = a.to(DEV), b.to(DEV)
+    c = oz.ozaki_matmul(ad, bd, num_splits=4, slice_dtype=torch.int8)
+    ref = ad @ bd
+    rel = ((c - ref).norm() / ref.norm()).item()
+    assert rel < 1e-8, rel
+    rows = np.array([0, 1, 127, 128, 4095, 8191])
+    cols = np.array([0, 63, 64, 1000, 8190, 8191])
+    want = oracle.ozaki_matmul(a.numpy()[rows], b.numpy()[:, cols], 4, "int8", "fp64")
+    assert same_bits(c.cpu().numpy()[np.ix_(rows, cols)], want)
