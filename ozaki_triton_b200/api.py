@@ -267,10 +267,12 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
               f"dot_accum={dot_accum_dtype}, out_accum={select_out_accum_dtype(input_dtype)}, "
               f"splits={num_splits}, alpha={alpha}")
 
+    if M == 0 or N == 0:
+        return torch.empty(out_shape, dtype=input_dtype, device=A.device)
     mode = _residual_mode(residual, num_splits, input_dtype)
     # split each distinct batch member once (no broadcast copies)
-    A3 = A.reshape(-1, M, K)
-    B3 = B.reshape(-1, K, N)
+    A3 = A.reshape(math.prod(a_batch), M, K)
+    B3 = B.reshape(math.prod(b_batch), K, N)
     # B is split by columns: lines = N (stride 1 when B is row-major), k stride = N
     b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), N, K, num_splits, alpha,
                               slice_dtype, mode)
@@ -280,16 +282,15 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     b_idx = _batch_index(b_batch, batch_shape, A.device)
 
     C = torch.empty((BN, M, N), dtype=input_dtype, device=A.device)
-    if M and N:
-        lib = _lib.load()
-        ld = a_sl.shape[-1]
-        _lib.check(lib.oz_cross_gemm(
-            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(),
-            BN, M, N, K, ld, num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[input_dtype],
-            a_idx.data_ptr() if a_idx is not None else None,
-            b_idx.data_ptr() if b_idx is not None else None,
-            A3.shape[0], B3.shape[0], C.data_ptr(), N,
-            _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0, _stream_ptr(A.device)))
+    lib = _lib.load()
+    ld = a_sl.shape[-1]
+    _lib.check(lib.oz_cross_gemm(
+        a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(),
+        BN, M, N, K, ld, num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[input_dtype],
+        a_idx.data_ptr() if a_idx is not None else None,
+        b_idx.data_ptr() if b_idx is not None else None,
+        A3.shape[0], B3.shape[0], C.data_ptr(), N,
+        _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0, _stream_ptr(A.device)))
     return C.view(out_shape)
 
 

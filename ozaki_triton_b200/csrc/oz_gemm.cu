@@ -27,17 +27,20 @@
 // TMEM and returns.
 
 #include <cstdio>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 
 #include "oz_common.cuh"
 
 namespace oz {
 
-constexpr int kBM = 128;          // rows per tile (UMMA M)
+constexpr int kBM = 128;          // rows per CTA (UMMA M per CTA)
 constexpr int kKBytes = 128;      // K bytes per pipeline stage (one swizzle row)
 constexpr int kGemmThreads = 320; // 10 warps
 constexpr int kEpiWarps = 8;
-constexpr int kStagesA = 4;
+constexpr int kMaxStages = 8;
+constexpr int kSmemBudget = 225 * 1024;   // stages + alignment slack
+constexpr int kBarrierBytes = 1024;
 
 struct GemmParams {
   const float *a_scales;
@@ -51,16 +54,19 @@ struct GemmParams {
   int skip_tail;
   int batch;
   int tiles_m, tiles_n, num_tiles;
-  uint32_t idesc;
+  int stages;            // pipeline depth
+  uint32_t idesc;        // instruction descriptor without the N field
 };
 
-template <int NT> struct GemmCfg {
-  static constexpr int kBBytes = NT * kKBytes;              // one B tile
-  static constexpr int kABytes = kBM * kKBytes;             // one A tile (16 KB)
-  static constexpr int kStagesB = (NT == 128) ? 8 : 12;
-  static constexpr int kSmemTiles = kStagesA * kABytes + kStagesB * kBBytes;
-  static constexpr int kSmemBytes = kSmemTiles + 1024 /*align*/ + 1024 /*barriers*/;
-};
+// One pipeline stage holds, for one 128-byte K block, the A tile of the pass
+// (128 rows of A_i) followed by the stacked B tiles of all s slices
+// (s x NT/PAIR rows: B_0 rows, B_1 rows, ...).  Stacking lets one MMA with
+// N = 256 cover several slices at once: its accumulator columns are the
+// products with consecutive B slices.
+__host__ __device__ constexpr int a_tile_bytes() { return kBM * kKBytes; }
+__host__ __device__ inline int stage_bytes(int s, int nt, int pair) {
+  return a_tile_bytes() + s * (nt / pair) * kKBytes;
+}
 
 template <int OUTK> struct OutT;
 template <> struct OutT<OZ_F64> { using acc = double; using store = double; };
@@ -83,12 +89,13 @@ to_out(typename OutT<OUTK>::acc v) {
   else return v;
 }
 
+// tile t -> (batch b, row tile mb, column tile nb) in a grouped raster:
+// GM row tiles sweep all column tiles before moving on, so the A rows and B
+// columns of the tiles running at the same time stay in L2.
 __device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, int &mb, int &nb) {
   const int tpb = p.tiles_m * p.tiles_n;
   b = t / tpb;
   int local = t - b * tpb;
-  // grouped raster: GM row-tiles sweep all column tiles before moving on,
-  // so the A rows and B columns of concurrently running tiles stay in L2
   constexpr int GM = 16;
   int per_group = GM * p.tiles_n;
   int group = local / per_group;
@@ -99,26 +106,42 @@ __device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, 
   nb = in_group / gsz;
 }
 
-template <int KIND, int OUTK, int NT>
+// PAIR == 1: one CTA computes a 128 x NT tile with cta_group::1 MMAs.
+// PAIR == 2: a cluster of two CTAs computes a 256 x NT tile; each CTA loads
+//            its 128 A rows and NT/2 rows of every B slice, the leader
+//            (rank 0) issues cta_group::2 MMAs over both CTAs' shared memory
+//            and each CTA's TMEM receives its own 128 rows.  Loads of both
+//            CTAs complete on the leader's "full" barriers; the leader's
+//            commits release the "empty" barriers and signal the
+//            accumulators of both CTAs.
+// TMEM layout of one pass: group g of up to 256 columns holds the products
+// with slices [g*SPG, g*SPG + SPG) (SPG = 256 / NT).  PAIR == 1: column
+// g*256 + jj*NT + x is slice g*SPG+jj, tile column x.  PAIR == 2: the first
+// Rg columns of a group come from the leader's B rows (tile columns
+// [0, NT/2)), the next Rg from the peer's (tile columns [NT/2, NT)), with
+// Rg = NT/2 * (slices in the group).
+template <int KIND, int OUTK, int NT, int PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     cross_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
-  using Cfg = GemmCfg<NT>;
   using ACC = typename OutT<OUTK>::acc;
   using STO = typename OutT<OUTK>::store;
-  constexpr int SB = Cfg::kStagesB;
+  constexpr int TM = kBM * PAIR;                  // rows of one tile
+  constexpr int R = NT / PAIR;                    // B rows per slice held by one CTA
+  constexpr int SPG = 256 / NT;                   // slices per MMA group
+  constexpr int NH = NT / 2;                      // tile columns per epilogue warp half
+
+  const int s = p.s;
+  const int S = p.stages;
+  const int sbytes = stage_bytes(s, NT, PAIR);
 
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   unsigned char *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  unsigned char *ring_a = smem;
-  unsigned char *ring_b = smem + kStagesA * Cfg::kABytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kSmemTiles);
-  uint64_t *full_a = bars;
-  uint64_t *empty_a = full_a + kStagesA;
-  uint64_t *full_b = empty_a + kStagesA;
-  uint64_t *empty_b = full_b + SB;
-  uint64_t *acc_full = empty_b + SB;      // [2]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * sbytes);
+  uint64_t *full = bars;                  // [S]
+  uint64_t *empty = full + kMaxStages;    // [S]
+  uint64_t *acc_full = empty + kMaxStages;  // [2]
   uint64_t *acc_empty = acc_full + 2;     // [2]
   uint64_t *drain = acc_empty + 2;        // [1]
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -126,17 +149,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int s = p.s;
   const int nbuf = (2 * s * NT <= 512) ? 2 : 1;
   int tcols = 32;
   while (tcols < nbuf * s * NT) tcols <<= 1;
+  const uint32_t rank = (PAIR == 2) ? cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int unit = blockIdx.x / PAIR;          // this CTA's pair (or CTA) index
+  const int units = gridDim.x / PAIR;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStagesA; ++i) { mbar_init(&full_a[i], 1); mbar_init(&empty_a[i], 1); }
-    for (int i = 0; i < SB; ++i) { mbar_init(&full_b[i], 1); mbar_init(&empty_b[i], 1); }
+    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiWarps * 32);
+      mbar_init(&acc_empty[i], PAIR * kEpiWarps * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -145,66 +170,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tm_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, (uint32_t)tcols);
-    tmem_relinquish();
+    if constexpr (PAIR == 2) {
+      tmem_alloc_pair(tmem_slot, (uint32_t)tcols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, (uint32_t)tcols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR == 2) cluster_sync();   // barriers of both CTAs initialised
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  // shared::cluster address of a barrier in the leader CTA
+  auto leader_addr = [&](uint64_t *bar) -> uint32_t {
+    if constexpr (PAIR == 2) return map_to_cta(smem_u32(bar), 0);
+    else return smem_u32(bar);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t ia = 0, ib = 0;   // running load counters (slot = counter % stages)
+      uint32_t it = 0;           // running stage counter (slot = it % S)
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+      const uint32_t tx = (uint32_t)(PAIR * sbytes);
+      for (int t = unit; ok && t < p.num_tiles; t += units) {
         int b, mb, nb;
         tile_coords(p, t, b, mb, nb);
         const int ai = p.a_index ? p.a_index[b] : b;
         const int bi = p.b_index ? p.b_index[b] : b;
+        const int arow = mb * TM + (int)rank * kBM;
+        const int brow = nb * NT + (int)rank * R;
         for (int i = 0; ok && i < s; ++i) {
-          const int js = p.skip_tail ? s - i : s;
-          for (int kb = 0; ok && kb < p.kblocks; ++kb) {
-            {
-              const int slot = ia % kStagesA;
-              const uint32_t par = ((ia / kStagesA) & 1) ^ 1;
-              if (!(ok = mbar_wait_bounded(&empty_a[slot], par, abort_flag, DEV_TIMEOUT_PRODUCER)))
-                break;
-              mbar_arrive_expect_tx(&full_a[slot], Cfg::kABytes);
-              tma_load_3d(ring_a + slot * Cfg::kABytes, &tm_a, &full_a[slot], kb * kKBytes,
-                          mb * kBM, ai * s + i);
-              ++ia;
-            }
-            for (int j = 0; j < js; ++j) {
-              const int slot = ib % SB;
-              const uint32_t par = ((ib / SB) & 1) ^ 1;
-              if (!(ok = mbar_wait_bounded(&empty_b[slot], par, abort_flag, DEV_TIMEOUT_PRODUCER)))
-                break;
-              mbar_arrive_expect_tx(&full_b[slot], Cfg::kBBytes);
-              tma_load_3d(ring_b + slot * Cfg::kBBytes, &tm_b, &full_b[slot], kb * kKBytes,
-                          nb * NT, bi * s + j);
-              ++ib;
+          for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+            const int slot = it % S;
+            if (!(ok = mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, abort_flag,
+                                         DEV_TIMEOUT_PRODUCER)))
+              break;
+            unsigned char *st = smem + slot * sbytes;
+            if constexpr (PAIR == 2) {
+              if (leader) mbar_arrive_expect_tx(&full[slot], tx);
+              const uint32_t fb = leader_addr(&full[slot]);
+              tma_load_3d_pair(st, &tm_a, fb, kb * kKBytes, arow, ai * s + i);
+              tma_load_3d_pair(st + a_tile_bytes(), &tm_b, fb, kb * kKBytes, brow, bi * s);
+            } else {
+              mbar_arrive_expect_tx(&full[slot], tx);
+              tma_load_3d(st, &tm_a, &full[slot], kb * kKBytes, arow, ai * s + i);
+              tma_load_3d(st + a_tile_bytes(), &tm_b, &full[slot], kb * kKBytes, brow, bi * s);
             }
           }
         }
       }
-      // drain: every issued load must have landed before shared memory is released
-      for (uint32_t k = (ia > kStagesA ? ia - kStagesA : 0); k < ia; ++k)
-        mbar_wait_bounded(&full_a[k % kStagesA], (k / kStagesA) & 1, abort_flag,
-                          DEV_TIMEOUT_PRODUCER);
-      for (uint32_t k = (ib > (uint32_t)SB ? ib - SB : 0); k < ib; ++k)
-        mbar_wait_bounded(&full_b[k % SB], (k / SB) & 1, abort_flag, DEV_TIMEOUT_PRODUCER);
+      // drain: every load the leader's barriers count must have landed
+      // before shared memory is released
+      if (leader)
+        for (uint32_t k = (it > (uint32_t)S ? it - S : 0); k < it; ++k)
+          mbar_wait_bounded(&full[k % S], (k / S) & 1, abort_flag, DEV_TIMEOUT_PRODUCER);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t ia = 0, ib = 0, pass = 0;
+    if (lane == 0 && leader) {
+      uint32_t it = 0, pass = 0;
       bool ok = true;
-      const uint32_t a_base = smem_u32(ring_a), b_base = smem_u32(ring_b);
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+      const uint32_t base = smem_u32(smem);
+      auto release = [&](uint64_t *bar) {
+        if constexpr (PAIR == 2) {
+          tc_commit_pair(smem_u32(bar));                     // own barrier
+          tc_commit_pair(map_to_cta(smem_u32(bar), 1));      // the peer's barrier
+        } else {
+          tc_commit(bar);
+        }
+      };
+      for (int t = unit; ok && t < p.num_tiles; t += units) {
         for (int i = 0; ok && i < s; ++i, ++pass) {
           const int js = p.skip_tail ? s - i : s;
+          const int groups = (js + SPG - 1) / SPG;
           const int buf = pass % nbuf;
           const uint32_t use = pass / nbuf;
           if (!(ok = mbar_wait_bounded(&acc_empty[buf], (use & 1) ^ 1, abort_flag,
@@ -212,60 +254,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           tc_fence_after();
           const uint32_t d0 = tmem_base + (uint32_t)(buf * s * NT);
-          for (int kb = 0; ok && kb < p.kblocks; ++kb) {
-            const int sa_slot = ia % kStagesA;
-            if (!(ok = mbar_wait_bounded(&full_a[sa_slot], (ia / kStagesA) & 1, abort_flag,
-                                         DEV_TIMEOUT_MMA)))
+          for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+            const int slot = it % S;
+            if (!(ok = mbar_wait_bounded(&full[slot], (it / S) & 1, abort_flag, DEV_TIMEOUT_MMA)))
               break;
-            tc_fence_after();
-            const uint64_t adesc = smem_desc_sw128(a_base + sa_slot * Cfg::kABytes);
-            for (int j = 0; j < js; ++j) {
-              const int sb_slot = ib % SB;
-              if (!(ok = mbar_wait_bounded(&full_b[sb_slot], (ib / SB) & 1, abort_flag,
-                                           DEV_TIMEOUT_MMA)))
-                break;
-              tc_fence_after();
-              const uint64_t bdesc = smem_desc_sw128(b_base + sb_slot * Cfg::kBBytes);
+            const uint32_t sa = base + slot * sbytes;
+            const uint64_t adesc = smem_desc_sw128(sa);
+#pragma unroll 1
+            for (int g = 0; g < groups; ++g) {
+              const int sg = min(SPG, js - g * SPG);
+              const uint32_t idesc = p.idesc | ((uint32_t)((sg * NT) >> 3) << 17);
+              const uint64_t bdesc =
+                  smem_desc_sw128(sa + a_tile_bytes() + g * (256 / PAIR) * kKBytes);
 #pragma unroll
               for (int kk = 0; kk < kKBytes / 32; ++kk) {
                 // advance 32 bytes along K inside the 128-byte swizzle row
-                tc_mma<KIND>(d0 + (uint32_t)(j * NT), adesc + (uint64_t)(kk * 2),
-                             bdesc + (uint64_t)(kk * 2), p.idesc, (kb | kk) != 0);
+                if constexpr (PAIR == 2)
+                  tc_mma_pair<KIND>(d0 + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
+                                    bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                else
+                  tc_mma<KIND>(d0 + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
+                               bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
               }
-              tc_commit(&empty_b[sb_slot]);
-              ++ib;
             }
-            if (!ok) break;
-            tc_commit(&empty_a[sa_slot]);
-            ++ia;
+            release(&empty[slot]);
           }
           if (!ok) break;
-          tc_commit(&acc_full[buf]);
+          release(&acc_full[buf]);
         }
       }
       // wait for all issued MMAs before TMEM / shared memory go away
-      tc_commit(drain);
+      if constexpr (PAIR == 2) tc_commit_pair(smem_u32(drain));
+      else tc_commit(drain);
       mbar_wait_bounded(drain, 0, abort_flag, DEV_TIMEOUT_MMA);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int e = warp - 2;
     const int sub = warp & 3;                 // TMEM lane quarter this warp may access
-    const int half = e >> 2;                  // which half of the NT columns
-    constexpr int NH = NT / 2;
-    const int row = sub * 32 + lane;
+    const int half = e >> 2;                  // which half of the NT tile columns
+    const int row = (int)rank * kBM + sub * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(sub * 32) << 16);
+    const uint32_t empty_addr0 = leader_addr(&acc_empty[0]);
+    const uint32_t empty_addr1 = leader_addr(&acc_empty[1]);
     ACC out[NH];
 #pragma unroll
     for (int x = 0; x < NH; ++x) out[x] = (ACC)0;
     uint32_t pass = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+    for (int t = unit; ok && t < p.num_tiles; t += units) {
       int b, mb, nb;
       tile_coords(p, t, b, mb, nb);
       const int ai = p.a_index ? p.a_index[b] : b;
       const int bi = p.b_index ? p.b_index[b] : b;
-      const int m = mb * kBM + row;
+      const int m = mb * TM + row;
       const int n0 = nb * NT + half * NH;
       for (int i = 0; i < s; ++i, ++pass) {
         const int js = p.skip_tail ? s - i : s;
@@ -279,15 +321,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         for (int j = 0; j < js; ++j) {
           const float *sbp = p.b_scales + ((int64_t)bi * s + j) * p.n;
+          const int g = j / SPG, jj = j % SPG;
+          int col;
+          if constexpr (PAIR == 2) {
+            const int rg = min(SPG, js - g * SPG) * NH;    // columns per CTA half in group
+            col = buf * s * NT + g * 256 + half * rg + jj * NH;
+          } else {
+            col = buf * s * NT + g * 256 + jj * NT + half * NH;
+          }
 #pragma unroll
           for (int c = 0; c < NH / 16; ++c) {
             uint32_t r[16];
-            tmem_ld16(lane_addr + (uint32_t)((buf * s + j) * NT + half * NH + c * 16), r);
+            tmem_ld16(lane_addr + (uint32_t)(col + c * 16), r);
             tmem_ld_wait();
 #pragma unroll
             for (int x = 0; x < 16; ++x) {
-              const int col = n0 + c * 16 + x;
-              const float sb = (col < p.n) ? __ldg(sbp + col) : 0.f;
+              const int cc = n0 + c * 16 + x;
+              const float sb = (cc < p.n) ? __ldg(sbp + cc) : 0.f;
               float v;
               if constexpr (KIND == 0) v = __int2float_rn((int)r[x]);
               else v = __uint_as_float(r[x]);
@@ -297,7 +347,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
+        if constexpr (PAIR == 2) {
+          if (leader) mbar_arrive(&acc_empty[buf]);
+          else mbar_arrive_remote(buf ? empty_addr1 : empty_addr0);
+        } else {
+          mbar_arrive(&acc_empty[buf]);
+        }
       }
       if (!ok) break;
       // store the finished tile
@@ -305,8 +360,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         STO *crow = reinterpret_cast<STO *>(p.c) + ((int64_t)b * p.m + m) * p.ldc;
 #pragma unroll
         for (int x = 0; x < NH; ++x) {
-          const int col = n0 + x;
-          if (col < p.n) crow[col] = to_out<OUTK>(out[x]);
+          const int cc = n0 + x;
+          if (cc < p.n) crow[cc] = to_out<OUTK>(out[x]);
         }
       }
 #pragma unroll
@@ -315,10 +370,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR == 2) cluster_sync();   // the peer's TMEM is written by the leader's MMAs
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, (uint32_t)tcols);
+    if constexpr (PAIR == 2) tmem_dealloc_pair(tmem_base, (uint32_t)tcols);
+    else tmem_dealloc(tmem_base, (uint32_t)tcols);
   }
 }
 
@@ -341,12 +398,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 int make_map(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows,
-             uint64_t mats, uint32_t box_rows) {
+             uint64_t mats, uint32_t box_rows, uint32_t box_mats) {
   auto enc = get_encode();
   if (!enc) return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {row_bytes, rows, mats};
   cuuint64_t strides[2] = {row_bytes, row_bytes * rows};
-  cuuint32_t box[3] = {(cuuint32_t)kKBytes, box_rows, 1};
+  cuuint32_t box[3] = {(cuuint32_t)kKBytes, box_rows, box_mats};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -355,7 +412,8 @@ int make_map(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t ro
   return OZ_OK;
 }
 
-uint32_t make_idesc(int slice_dtype, int nt) {
+// Instruction descriptor without the N field (bits 17-22, set per MMA group).
+uint32_t make_idesc(int slice_dtype, int mt) {
   uint32_t c_fmt, ab_fmt;
   switch (slice_dtype) {
     case OZ_I8: c_fmt = 2; ab_fmt = 1; break;    // S32 accumulate, signed 8-bit
@@ -368,8 +426,7 @@ uint32_t make_idesc(int slice_dtype, int nt) {
   d |= ab_fmt << 7;
   d |= ab_fmt << 10;
   // bits 15/16 = 0: both operands K-major
-  d |= (uint32_t)(nt >> 3) << 17;
-  d |= (uint32_t)(kBM >> 4) << 24;
+  d |= (uint32_t)(mt >> 4) << 24;
   return d;
 }
 
@@ -384,30 +441,69 @@ int sm_count() {
   return n;
 }
 
-template <int KIND, int OUTK, int NT>
+template <int KIND, int OUTK, int NT, int PAIR>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
                 cudaStream_t st) {
-  using Cfg = GemmCfg<NT>;
-  auto kern = cross_gemm_kernel<KIND, OUTK, NT>;
+  auto kern = cross_gemm_kernel<KIND, OUTK, NT, PAIR>;
+  const int smem = p.stages * stage_bytes(p.s, NT, PAIR) + 1024 + kBarrierBytes;
   if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               Cfg::kSmemBytes),
+                                               smem),
                           "cudaFuncSetAttribute(cross_gemm)"))
     return rc;
-  int grid = min(p.num_tiles, sm_count());
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
-  return check_cuda(cudaGetLastError(), "cross_gemm_kernel launch");
+  const int units = min(p.num_tiles, sm_count() / PAIR);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(units * PAIR));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, p), "cross_gemm_kernel launch");
 }
 
-template <int KIND, int NT>
+template <int KIND, int NT, int PAIR>
 int launch_out(int out_dtype, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
                cudaStream_t st) {
   switch (out_dtype) {
-    case OZ_F64: return launch_gemm<KIND, OZ_F64, NT>(ta, tb, p, st);
-    case OZ_F32: return launch_gemm<KIND, OZ_F32, NT>(ta, tb, p, st);
-    case OZ_F16: return launch_gemm<KIND, OZ_F16, NT>(ta, tb, p, st);
-    case OZ_BF16: return launch_gemm<KIND, OZ_BF16, NT>(ta, tb, p, st);
+    case OZ_F64: return launch_gemm<KIND, OZ_F64, NT, PAIR>(ta, tb, p, st);
+    case OZ_F32: return launch_gemm<KIND, OZ_F32, NT, PAIR>(ta, tb, p, st);
+    case OZ_F16: return launch_gemm<KIND, OZ_F16, NT, PAIR>(ta, tb, p, st);
+    case OZ_BF16: return launch_gemm<KIND, OZ_BF16, NT, PAIR>(ta, tb, p, st);
   }
   return set_error(OZ_ERR_UNSUPPORTED, "unsupported output dtype %d", out_dtype);
+}
+
+template <int NT, int PAIR>
+int launch_kind(int kind, int out_dtype, const CUtensorMap &ta, const CUtensorMap &tb,
+                const GemmParams &p, cudaStream_t st) {
+  if (kind == 0) return launch_out<0, NT, PAIR>(out_dtype, ta, tb, p, st);
+  if (kind == 1) return launch_out<1, NT, PAIR>(out_dtype, ta, tb, p, st);
+  return launch_out<2, NT, PAIR>(out_dtype, ta, tb, p, st);
+}
+
+// The tile table (it replaces the reference's Optuna autotuner): NT columns
+// per tile so that the s accumulators of one pass fit the 512 TMEM columns,
+// and CTA pairs (256-row tiles, half the B traffic per CTA) unless M fits one
+// 128-row tile.  OZ_GEMM_TILE="pair,nt" overrides it (benchmarking only).
+struct TileChoice { int pair, nt; };
+TileChoice choose_tile(int64_t m, int s) {
+  TileChoice t;
+  t.nt = s <= 4 ? 128 : 64;
+  t.pair = m > kBM ? 2 : 1;
+  if (const char *env = getenv("OZ_GEMM_TILE")) {
+    int pr = 0, nt = 0;
+    if (sscanf(env, "%d,%d", &pr, &nt) == 2 && (pr == 1 || pr == 2) && (nt == 64 || nt == 128) &&
+        s * nt <= 512) {
+      t.pair = pr;
+      t.nt = nt;
+    }
+  }
+  return t;
 }
 
 }  // namespace
@@ -460,13 +556,16 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
       b_batches * num_splits > INT32_MAX)
     return set_error(OZ_ERR_INVALID, "size out of range");
 
-  const int nt = num_splits <= 4 ? 128 : 64;
+  const TileChoice tc = choose_tile(m, num_splits);
+  const int nt = tc.nt, pair = tc.pair;
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, a_slices, (uint64_t)ld_bytes, (uint64_t)m,
-                        (uint64_t)(a_batches * num_splits), kBM))
+                        (uint64_t)(a_batches * num_splits), kBM, 1))
     return rc;
+  // B: one box = the K block of all num_splits slices, stacked
   if (int rc = make_map(&tb, b_slices, (uint64_t)ld_bytes, (uint64_t)n,
-                        (uint64_t)(b_batches * num_splits), (uint32_t)nt))
+                        (uint64_t)(b_batches * num_splits), (uint32_t)(nt / pair),
+                        (uint32_t)num_splits))
     return rc;
 
   GemmParams p;
@@ -482,20 +581,19 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
   p.s = num_splits;
   p.skip_tail = (flags & OZ_GEMM_SKIP_TAIL) ? 1 : 0;
   p.batch = (int)batch;
-  p.tiles_m = (int)((m + kBM - 1) / kBM);
+  p.tiles_m = (int)((m + kBM * pair - 1) / (kBM * pair));
   p.tiles_n = (int)((n + nt - 1) / nt);
   int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
-  p.idesc = make_idesc(slice_dtype, nt);
+  p.idesc = make_idesc(slice_dtype, kBM * pair);
+  p.stages = min(kMaxStages, kSmemBudget / stage_bytes(num_splits, nt, pair));
 
   const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
-  if (nt == 128) {
-    if (kind == 0) return launch_out<0, 128>(out_dtype, ta, tb, p, st);
-    if (kind == 1) return launch_out<1, 128>(out_dtype, ta, tb, p, st);
-    return launch_out<2, 128>(out_dtype, ta, tb, p, st);
+  if (pair == 2) {
+    if (nt == 128) return launch_kind<128, 2>(kind, out_dtype, ta, tb, p, st);
+    return launch_kind<64, 2>(kind, out_dtype, ta, tb, p, st);
   }
-  if (kind == 0) return launch_out<0, 64>(out_dtype, ta, tb, p, st);
-  if (kind == 1) return launch_out<1, 64>(out_dtype, ta, tb, p, st);
-  return launch_out<2, 64>(out_dtype, ta, tb, p, st);
+  if (nt == 128) return launch_kind<128, 1>(kind, out_dtype, ta, tb, p, st);
+  return launch_kind<64, 1>(kind, out_dtype, ta, tb, p, st);
 }
