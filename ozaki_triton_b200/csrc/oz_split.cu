@@ -31,9 +31,13 @@
 //                       (s + 1 reads of the line); used only when the two
 //                       fast kernels do not apply.
 
+#include <algorithm>
 #include <cstdio>
+#include <type_traits>
+#include <cudaTypedefs.h>
 
 #include "oz_common.cuh"
+#include "oz_log2_table.h"
 
 namespace oz {
 
@@ -142,174 +146,508 @@ template <> __device__ __forceinline__ float abs_to_f32<float>(float v) { return
 template <typename T, int N> struct alignas(sizeof(T) * N) Pack { T e[N]; };
 
 // ---------------------------------------------------------------------------
-// rows: the split axis is contiguous
+// fast per-level quantisation for the streaming kernels
+//
+// Level 0 of an fp64 input (and every level in OZ_RESIDUAL_EXACT mode) works
+// on the fp64 residual.  After level 0 the reference's residual is an fp32
+// value (its residual buffer is fp32), so levels >= 1 run in fp32 registers:
+// x = r * 2^-e is then exact, and the reference's fp64 "x + 0.5, truncate"
+// equals exact rounding half away from zero (x + 0.5 needs at most 33 bits
+// whenever the result can be nonzero).  Inputs other than fp64 have an fp32
+// residual from the start and follow the reference's fp32 arithmetic
+// (x + 0.5 rounded to fp32, then truncated).  Rounding to an integer uses the
+// 1.5 * 2^23 (fp32) / 1.5 * 2^52 (fp64) magic-number identities instead of
+// conversion instructions where that is exact.
 // ---------------------------------------------------------------------------
-constexpr int kRowThreads = 256;
+// ceil(float32(log2(m))) for positive float32 m (ozaki_triton.py:174): the
+// binade's exponent plus one once the mantissa reaches the binade's
+// threshold (oz_log2_table.h); subnormal m (the 1e-38 floor) take the
+// float64 log2 route.
+__device__ __forceinline__ int ceil_log2_table(float m) {
+  const uint32_t b = __float_as_uint(m);
+  const uint32_t B = b >> 23;
+  if (B == 0) return ceil_log2_f32(m);
+  return (int)B - 127 + ((int)(b & 0x7FFFFFu) >= kCeilLog2Thr[B] ? 1 : 0);
+}
 
-template <typename TIn, int SK, int VEC, int NCH, bool EXACT>
-__global__ void __launch_bounds__(kRowThreads)
-    split_rows_kernel(const TIn *__restrict__ in, int64_t stride_b, int64_t stride_line, int lines,
-                      int K, int ld, int s, int alpha, typename SliceT<SK>::type *__restrict__ out,
-                      float *__restrict__ scales, int T) {
-  using RD = typename RdOf<TIn>::type;
-  using ST = typename SliceT<SK>::type;
-  __shared__ float red[2][kRowThreads / 32];
-
-  const int lpb = kRowThreads / T;                 // lines per block
-  const int grp = threadIdx.x / T;
-  const int tl = threadIdx.x % T;                  // thread within the line group
-  const int line = blockIdx.x * lpb + grp;
-  const int b = blockIdx.y;
-  const bool active = line < lines;
-
-  RD v[NCH][VEC];
-  const TIn *src = in + (int64_t)b * stride_b + (int64_t)(active ? line : 0) * stride_line;
-#pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) {
-    int k0 = (ch * T + tl) * VEC;
-    if (active && k0 < K) {
-      if constexpr (VEC > 1) {
-        Pack<TIn, VEC> p = *reinterpret_cast<const Pack<TIn, VEC> *>(src + k0);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) v[ch][e] = in_to_rd<TIn, RD>(p.e[e]);
-      } else {
-        v[ch][0] = in_to_rd<TIn, RD>(src[k0]);
-      }
+struct LevelP {
+  float scale;      // stored scale 2^e
+  double inv_d;     // 2^-e
+  float inv1, inv2; // 2^-e == inv1 * inv2, both exact floats
+  __device__ __forceinline__ void init(float row_max, int alpha) {
+    const float m = fmaxf(1e-38f, row_max);
+    const int e = ceil_log2_table(m) - alpha;     // e in [-149, 127]
+    scale = pow2f(e);
+    inv_d = pow2d(-e);
+    if (-e > 127) {
+      inv1 = 18446744073709551616.0f;             // 2^64
+      inv2 = pow2f(-e - 64);
     } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) v[ch][e] = (RD)0;
+      inv1 = 1.0f;
+      inv2 = pow2f(-e);
     }
   }
+};
 
-  ST *dst_base = out + ((int64_t)b * s * lines + (active ? line : 0)) * (int64_t)ld;
-  for (int l = 0; l < s; ++l) {
-    // ---- line max of |res| (max commutes with the monotone rd->fp32 rounding)
-    float m = 0.f;
-#pragma unroll
-    for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) m = fmaxf(m, abs_to_f32<RD>(v[ch][e]));
-    const int w = (T < 32) ? T : 32;
-    for (int o = w / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (T > 32) {
-      if ((threadIdx.x & 31) == 0) red[l & 1][threadIdx.x >> 5] = m;
-      __syncthreads();
-      const int nw = T / 32, w0 = (grp * T) / 32;
-      m = red[l & 1][w0];
-      for (int i = 1; i < nw; ++i) m = fmaxf(m, red[l & 1][w0 + i]);
-    }
-    Level<RD> lv;
-    lv.init(m, alpha);
-    if (active && tl == 0) scales[((int64_t)b * s + l) * lines + line] = lv.scale;
+constexpr float kMagicF = 12582912.0f;            // 1.5 * 2^23
+constexpr int kMagicFBits = 0x4B400000;
 
-    ST *dst = dst_base + (int64_t)l * lines * ld;
-    const bool upd = l < s - 1;
+// exact float(n) for |n| < 2^22
+__device__ __forceinline__ float small_int_to_float(int n) {
+  return __fsub_rn(__int_as_float(n + kMagicFBits), kMagicF);
+}
+// exact double(n) for any 32-bit n: 1.5 * 2^52 + n, minus 1.5 * 2^52
+__device__ __forceinline__ double int_to_double_exact(int n) {
+  return __dsub_rn(__hiloint2double(0x43380000 + (n >> 31), n), 6755399441055744.0);
+}
+__device__ __forceinline__ int clamp_i8(int n) { return max(-128, min(127, n)); }
+
+template <int SK> __device__ __forceinline__ typename SliceT<SK>::type slice_from_f64(double x) {
+  if constexpr (SK == OZ_F16) {
+    unsigned short h;
+    asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(x));
+    return __ushort_as_half(h);
+  } else if constexpr (SK == OZ_BF16) {
+    unsigned short h;
+    asm("cvt.rn.bf16.f64 %0, %1;" : "=h"(h) : "d"(x));
+    return __ushort_as_bfloat16(h);
+  } else {
+    return __double2float_rn(x);
+  }
+}
+template <int SK> __device__ __forceinline__ typename SliceT<SK>::type slice_from_f32(float x) {
+  if constexpr (SK == OZ_F16) return __float2half_rn(x);
+  else if constexpr (SK == OZ_BF16) return __float2bfloat16_rn(x);
+  else return x;
+}
+template <int SK> __device__ __forceinline__ float slice_to_f32(typename SliceT<SK>::type q) {
+  if constexpr (SK == OZ_F16) return __half2float(q);
+  else if constexpr (SK == OZ_BF16) return __bfloat162float(q);
+  else return q;
+}
+
+// level on an fp64 residual; the next residual goes to rn_d (EXACT) or,
+// rounded to fp32 like the reference's residual buffer, to rn_f
+template <int SK, bool EXACT>
+__device__ __forceinline__ typename SliceT<SK>::type step_f64(double r, const LevelP &lv, bool upd,
+                                                              double &rn_d, float &rn_f) {
+  const double x = __dmul_rn(r, lv.inv_d);
+  double qd;
+  typename SliceT<SK>::type q;
+  if constexpr (SK == OZ_I8) {
+    const double t = __dadd_rn(x, copysign(0.5, x));
+    const int n = clamp_i8(__double2int_rz(t));
+    q = (int8_t)n;
+    qd = int_to_double_exact(n);
+  } else {
+    q = slice_from_f64<SK>(x);
+    qd = (double)slice_to_f32<SK>(q);
+  }
+  if (upd) {
+    // q * scale is exact, so one fused rounding equals the reference's r - q*s
+    const double d = __fma_rn(-qd, (double)lv.scale, r);
+    if constexpr (EXACT) rn_d = d;
+    else rn_f = __double2float_rn(d);
+  }
+  return q;
+}
+
+// Integer rounding of a = min(|x|, 130) as a float holding
+// floor(a + 0.5) + 1.5 * 2^23, clamped to 127 (x >= 0) / 128 (x < 0).
+// fl32(a + 0.5) has the floor of the exact sum for every fp32 a except
+// 0.5 - 2^-25 (checked exhaustively over all fp32 values below 512): that
+// one input is folded to 0 when EXACT_HALF (fp64 reference arithmetic) and
+// kept (fp32 reference arithmetic rounds it up) otherwise.  Pre-clamping |x|
+// to 130 changes no result (the reference saturates beyond 128) and keeps
+// the magic-number rounding exact for any alpha.
+template <bool EXACT_HALF>
+__device__ __forceinline__ float round_half_away_magic(float a, bool neg) {
+  const float t = __fadd_rn(a, 0.5f);
+  float y = __fadd_rn(t, kMagicF);                        // nearest integer of t, + M
+  y = (__fsub_rn(y, kMagicF) > t) ? __fsub_rn(y, 1.0f) : y;   // -> floor(t) + M
+  if (EXACT_HALF) y = (a == __int_as_float(0x3EFFFFFF)) ? kMagicF : y;
+  return fminf(y, neg ? kMagicF + 128.0f : kMagicF + 127.0f);
+}
+
+// level >= 1 of an fp64 input (fp32-valued residual, fp64 reference arithmetic)
+template <int SK>
+__device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, const LevelP &lv,
+                                                                    bool upd) {
+  const float x = __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);   // exact
+  if constexpr (SK == OZ_I8) {
+    const bool neg = x < 0.f;
+    const float y = round_half_away_magic<true>(fminf(fabsf(x), 130.f), neg);
+    const float qa = __fsub_rn(y, kMagicF);                    // |q| as float
+    const int na = __float_as_int(y) - kMagicFBits;            // |q|
+    if (upd) r = __fmaf_rn(-copysignf(qa, x), lv.scale, r);
+    return (int8_t)(neg ? -na : na);
+  } else {
+    const auto q = slice_from_f32<SK>(x);
+    if (upd) r = __fmaf_rn(-slice_to_f32<SK>(q), lv.scale, r);
+    return q;
+  }
+}
+
+// every level of a non-fp64 input (fp32 residual, fp32 reference arithmetic)
+template <int SK>
+__device__ __forceinline__ typename SliceT<SK>::type step_f32_rd(float &r, const LevelP &lv,
+                                                                 bool upd) {
+  const float x = __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);   // == r / scale, rounded once
+  if constexpr (SK == OZ_I8) {
+    // trunc(fl32(x +- 0.5)) == sign(x) * floor(fl32(|x| + 0.5))
+    const bool neg = x < 0.f;
+    const float y = round_half_away_magic<false>(fminf(fabsf(x), 130.f), neg);
+    const float qa = __fsub_rn(y, kMagicF);
+    const int na = __float_as_int(y) - kMagicFBits;
+    if (upd) r = __fsub_rn(r, __fmul_rn(copysignf(qa, x), lv.scale));
+    return (int8_t)(neg ? -na : na);
+  } else {
+    const auto q = slice_from_f32<SK>(x);
+    if (upd) r = __fsub_rn(r, __fmul_rn(slice_to_f32<SK>(q), lv.scale));
+    return q;
+  }
+}
+
+// bulk (non-tensor) TMA copy global -> shared, completion counted on `bar`
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_plain(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                                  int c0, int c1, int c2) {
+  tma_load_3d(dst, map, bar, c0, c1, c2);
+}
+
+// Per-thread storage of one line's values and the level loop, shared by the
+// streaming kernels.  NV values per thread; `emit(l, idx, q)` stores slice
+// element idx of level l; `reduce(m, l)` returns the line max over the
+// threads of the line.
+template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
+  using ST = typename SliceT<SK>::type;
+  static constexpr bool F64IN = sizeof(TIn) == 8;
+  double vd[F64IN ? NV : 1];
+  float vf[NV];
+
+  __device__ __forceinline__ void set(int i, TIn v) {
+    if constexpr (F64IN) vd[i] = v;
+    else vf[i] = InTraits<TIn>::to_float(v);
+  }
+
+  template <typename Reduce, typename Emit, typename Scale>
+  __device__ __forceinline__ void run(int s, int alpha, Reduce reduce, Emit emit, Scale put_scale) {
+    for (int l = 0; l < s; ++l) {
+      const bool upd = l < s - 1;
+      const bool on_f64 = F64IN && (EXACT || l == 0);
+      float m;
+      if (on_f64) {
+        double md = 0.0;
 #pragma unroll
-    for (int ch = 0; ch < NCH; ++ch) {
-      int k0 = (ch * T + tl) * VEC;
-      Pack<ST, VEC> q;
+        for (int i = 0; i < NV; ++i) md = fmax(md, fabs(vd[i]));
+        m = __double2float_rn(md);
+      } else {
+        m = 0.f;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) q.e[e] = quant_step<SK, RD, EXACT>(v[ch][e], lv, upd);
-      if (active && k0 < ld) *reinterpret_cast<Pack<ST, VEC> *>(dst + k0) = q;
+        for (int i = 0; i < NV; ++i) m = fmaxf(m, fabsf(vf[i]));
+      }
+      m = reduce(m, l);
+      LevelP lv;
+      lv.init(m, alpha);
+      put_scale(l, lv.scale);
+      if (on_f64) {
+        if constexpr (F64IN) {
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            double nd = 0.0;
+            float nf = 0.f;
+            ST q = step_f64<SK, EXACT>(vd[i], lv, upd, nd, nf);
+            if constexpr (EXACT) vd[i] = nd;
+            else vf[i] = nf;
+            emit(l, i, q);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          ST q;
+          if constexpr (F64IN) q = step_f32_exact<SK>(vf[i], lv, upd);
+          else q = step_f32_rd<SK>(vf[i], lv, upd);
+          emit(l, i, q);
+        }
+      }
     }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// rows: the split axis is contiguous (rows of A)
+// ---------------------------------------------------------------------------
+constexpr int kRowCTA = 512;
+constexpr int kRowMaxStages = 4;
+constexpr int kRowSmem = 200 * 1024;
+
+// Persistent kernel: each iteration takes RPS = 512 / T whole rows; a group
+// of T threads owns a row.  Rows arrive by bulk TMA copies into a ring of NS
+// stages, are moved to registers, and the stage is refilled with a later
+// iteration's rows while the levels are computed.  Thread `tl` of a row
+// holds elements [(c*T + tl)*VEC, +VEC) for c < NCH (16-byte chunks: the
+// shared-memory reads are conflict-free and the slice stores coalesce).
+template <typename TIn, int SK, int T, int NCH, bool EXACT>
+__global__ void __launch_bounds__(kRowCTA, 1)
+    split_rows_tma(const TIn *__restrict__ in, int64_t stride_b, int64_t stride_line, int lines,
+                   int64_t total, int K, int ld, int s, int alpha,
+                   typename SliceT<SK>::type *__restrict__ out, float *__restrict__ scales, int NS,
+                   int rowp) {
+  using ST = typename SliceT<SK>::type;
+  constexpr int VEC = 16 / (int)sizeof(TIn);
+  constexpr int NV = NCH * VEC;
+  constexpr int RPS = kRowCTA / T;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int stage = RPS * rowp;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + NS * stage);
+  float *red = reinterpret_cast<float *>(full + kRowMaxStages);   // [2][16]
+  const int grp = threadIdx.x / T, tl = threadIdx.x % T;
+  const int64_t groups = (total + RPS - 1) / RPS;
+  const uint32_t row_bytes = (uint32_t)K * (uint32_t)sizeof(TIn);
+
+  auto issue = [&](int64_t g, int st) {
+    int nrows = (int)min((int64_t)RPS, total - g * RPS);
+    mbar_arrive_expect_tx(&full[st], (uint32_t)nrows * row_bytes);
+    for (int r = 0; r < nrows; ++r) {
+      const int64_t row = g * RPS + r;
+      const int64_t b = row / lines, line = row % lines;
+      bulk_load(smem + st * stage + r * rowp, in + b * stride_b + line * stride_line, row_bytes,
+                &full[st]);
+    }
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < NS && blockIdx.x + (int64_t)i * gridDim.x < groups; ++i)
+      issue(blockIdx.x + (int64_t)i * gridDim.x, i);
+
+  // which of this thread's chunks lie inside the row pitch (written), and
+  // inside K (read); fixed for the whole kernel
+  uint32_t in_ld = 0, in_k = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int k0 = (c * T + tl) * VEC;
+    in_ld |= (uint32_t)(k0 < ld) << c;
+    in_k |= (uint32_t)(k0 < K) << c;
+  }
+
+  volatile int abort_flag = 0;
+  int it = 0;
+  for (int64_t g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+    const int st = it % NS;
+    // a timeout is recorded and the loop keeps going so that every thread
+    // reaches the same barriers; the output is then reported as undefined
+    mbar_wait_bounded(&full[st], (it / NS) & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_PRODUCER);
+    const int64_t row = g * RPS + grp;
+    const bool active = row < total;
+    LineLevels<TIn, SK, NV, EXACT> ll;
+    const TIn *srow = reinterpret_cast<const TIn *>(smem + st * stage + grp * rowp) + tl * VEC;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      Pack<TIn, VEC> pk;
+      if (active && ((in_k >> c) & 1)) pk = *reinterpret_cast<const Pack<TIn, VEC> *>(srow + c * T * VEC);
+      else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) pk.e[e] = (TIn)0.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) ll.set(c * VEC + e, pk.e[e]);
+    }
+    __syncthreads();                       // stage consumed by every thread
+    if (threadIdx.x == 0) {
+      const int64_t gn = g + (int64_t)NS * gridDim.x;
+      if (gn < groups) issue(gn, st);
+    }
+    const int64_t b = active ? row / lines : 0, line = active ? row % lines : 0;
+    ST *dst = out + (b * s * lines + line) * (int64_t)ld + tl * VEC;
+    const uint32_t wmask = active ? in_ld : 0u;
+    const int64_t level_stride = (int64_t)lines * ld;
+    auto reduce = [&](float m, int l) -> float {
+      constexpr int w = T < 32 ? T : 32;
+#pragma unroll
+      for (int o = w / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if constexpr (T > 32) {
+        if ((threadIdx.x & 31) == 0) red[(l & 1) * 16 + (threadIdx.x >> 5)] = m;
+        __syncthreads();
+        constexpr int nw = T / 32;
+        const int lane = threadIdx.x & 31;
+        float v = lane < nw ? red[(l & 1) * 16 + (grp * T) / 32 + lane] : 0.f;
+#pragma unroll
+        for (int o = nw / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        m = __shfl_sync(0xffffffffu, v, 0);
+      }
+      return m;
+    };
+    auto put_scale = [&](int l, float sc) {
+      if (active && tl == 0) scales[(b * s + l) * lines + line] = sc;
+    };
+    // slices are stored VEC elements at a time
+    Pack<ST, VEC> pq;
+    ST *dl = dst;
+    int cur_l = -1;
+    auto emit = [&](int l, int i, ST q) {
+      if (l != cur_l) { dl = dst + l * level_stride; cur_l = l; }
+      pq.e[i % VEC] = q;
+      if (i % VEC == VEC - 1) {
+        const int c = i / VEC;
+        if ((wmask >> c) & 1) *reinterpret_cast<Pack<ST, VEC> *>(dl + c * T * VEC) = pq;
+      }
+    };
+    ll.run(s, alpha, reduce, emit, put_scale);
   }
 }
 
 // ---------------------------------------------------------------------------
-// columns: the lines are contiguous, the split axis is strided
+// columns: the lines are contiguous, the split axis is strided (columns of B)
 // ---------------------------------------------------------------------------
-constexpr int kColThreads = 256;
+constexpr int kColCTA = 512;
 constexpr int kMaxCluster = 8;
+constexpr int kColSmem = 200 * 1024;
 
-template <typename TIn, int SK, int W, int V, bool EXACT>
-__global__ void __launch_bounds__(kColThreads)
-    split_cols_kernel(const TIn *__restrict__ in, int64_t stride_b, int64_t stride_k, int lines,
-                      int K, int ld, int s, int alpha, typename SliceT<SK>::type *__restrict__ out,
-                      float *__restrict__ scales) {
-  using RD = typename RdOf<TIn>::type;
+// Persistent cluster kernel: a cluster of CL CTAs owns one panel of W columns
+// (W * sizeof(TIn) = 64 bytes) at a time; CTA `rank` holds K rows
+// [rank*KC, rank*KC + KC) of it, KC = G * V with G = 512 / W row groups.
+// Panels arrive by TMA tiles into a ring of NS stages; per-level column
+// maxima are combined across the cluster through distributed shared memory;
+// slices are transposed in shared memory and written K-contiguous.
+template <typename TIn, int SK, int V, bool EXACT>
+__global__ void __launch_bounds__(kColCTA, 1)
+    split_cols_tma(const __grid_constant__ CUtensorMap tm_in, int lines, int batch, int K,
+                   int ld, int s, int alpha, typename SliceT<SK>::type *__restrict__ out,
+                   float *__restrict__ scales, int NS) {
   using ST = typename SliceT<SK>::type;
-  constexpr int G = kColThreads / W;                 // row groups
-  constexpr int KC = G * V;                          // rows of K per CTA
-  constexpr int PITCH = KC * (int)sizeof(ST) + 16;   // staging row pitch in bytes
+  constexpr int W = 64 / (int)sizeof(TIn);
+  constexpr int G = kColCTA / W;
+  constexpr int KC = G * V;
+  constexpr int BOXR = KC < 256 ? KC : 256;
+  constexpr int STAGE = KC * 64;
+  constexpr int PITCH = KC * (int)sizeof(ST) + 16;   // staging row pitch, bytes
   static_assert(V % 4 == 0, "V must be a multiple of 4");
 
-  extern __shared__ __align__(16) unsigned char smem[];
-  float *red = reinterpret_cast<float *>(smem);                 // [G][W]
-  float *peer = red + G * W;                                    // [2][kMaxCluster][W]
-  unsigned char *stage = smem + ((G * W + 2 * kMaxCluster * W) * 4 + 15) / 16 * 16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char *outst = smem + NS * STAGE;                         // [W][PITCH]
+  float *red = reinterpret_cast<float *>(outst + W * PITCH);        // [G][W]
+  float *peer = red + G * W;                                        // [2][kMaxCluster][W]
+  uint64_t *full = reinterpret_cast<uint64_t *>(peer + 2 * kMaxCluster * W);
+  uint64_t *xbar = full + 4;            // per-level exchange of column maxima
 
   const int CL = (int)cluster_nctarank();
   const int rank = (int)cluster_ctarank();
-  const int panel = blockIdx.x / CL;
-  const int b = blockIdx.y;
-  const int c = threadIdx.x % W;
-  const int g = threadIdx.x / W;
-  const int n = panel * W + c;
-  const bool col_ok = n < lines;
+  const int cid = blockIdx.x / CL, ncl = gridDim.x / CL;
+  const int npan = (lines + W - 1) / W;
+  const int64_t work = (int64_t)npan * batch;
+  const int c = threadIdx.x % W, g = threadIdx.x / W;
   const int kbase = rank * KC;
 
-  RD v[V / 4][4];
-  const TIn *src = in + (int64_t)b * stride_b + (col_ok ? n : 0);
-#pragma unroll
-  for (int i = 0; i < V / 4; ++i)
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int k = kbase + 4 * (g + G * i) + u;
-      v[i][u] = (col_ok && k < K) ? in_to_rd<TIn, RD>(src[(int64_t)k * stride_k]) : (RD)0;
-    }
+  auto issue = [&](int64_t pw, int st) {
+    const int b = (int)(pw / npan), pn = (int)(pw % npan);
+    mbar_arrive_expect_tx(&full[st], STAGE);
+    for (int r0 = 0; r0 < KC; r0 += BOXR)
+      tma_load_3d(smem + st * STAGE + r0 * 64, &tm_in, &full[st], pn * W, kbase + r0, b);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tm_in);
+  }
+  if (CL > 1) cluster_sync();   // peers' barriers exist before any remote store
+  else __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < NS && cid + (int64_t)i * ncl < work; ++i) issue(cid + (int64_t)i * ncl, i);
+  uint32_t lc = 0;              // levels exchanged so far (exchange barrier phase)
 
-  for (int l = 0; l < s; ++l) {
-    float m = 0.f;
+  volatile int abort_flag = 0;
+  int it = 0;
+  for (int64_t pw = cid; pw < work; pw += ncl, ++it) {
+    const int st = it % NS;
+    // a timeout here is recorded and the loop keeps going: the cluster must
+    // stay in step, and the output is reported as undefined by the status
+    mbar_wait_bounded(&full[st], (it / NS) & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_PRODUCER);
+    const int b = (int)(pw / npan), pn = (int)(pw % npan);
+    const int n = pn * W + c;
+    const bool col_ok = n < lines;
+    LineLevels<TIn, SK, V, EXACT> ll;
+    const TIn *sp = reinterpret_cast<const TIn *>(smem + st * STAGE);
 #pragma unroll
     for (int i = 0; i < V / 4; ++i)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) m = fmaxf(m, abs_to_f32<RD>(v[i][u]));
-    red[g * W + c] = m;
-    __syncthreads();
-    if (threadIdx.x < W) {
-      float mm = red[threadIdx.x];
-      for (int gg = 1; gg < G; ++gg) mm = fmaxf(mm, red[gg * W + threadIdx.x]);
-      float *slot = peer + ((l & 1) * kMaxCluster + rank) * W + threadIdx.x;
-      if (CL > 1) {
-        uint32_t a = smem_u32(slot);
-        for (int r = 0; r < CL; ++r) st_cluster_f32(map_to_cta(a, r), mm);
-      } else {
-        *slot = mm;
+      for (int u = 0; u < 4; ++u) ll.set(i * 4 + u, sp[(4 * (g + G * i) + u) * W + c]);
+    __syncthreads();                       // stage consumed by every thread
+    if (threadIdx.x == 0) {
+      const int64_t pn2 = pw + (int64_t)NS * ncl;
+      if (pn2 < work) issue(pn2, st);
+    }
+    // Column maxima: CTA-local reduction, then every CTA sends its W partial
+    // maxima to every CTA of the cluster with asynchronous remote stores that
+    // complete on the receiver's exchange barrier (no cluster-wide barrier
+    // per level).  Slots are double-buffered by level parity: a CTA can only
+    // be one level ahead of a peer that still reads the other buffer.
+    auto reduce = [&](float m, int l) -> float {
+      (void)l;
+      const int pb = (int)(lc & 1);
+      red[g * W + c] = m;
+      __syncthreads();
+      if (threadIdx.x < W) {
+        float mm = red[threadIdx.x];
+        for (int gg = 1; gg < G; ++gg) mm = fmaxf(mm, red[gg * W + threadIdx.x]);
+        float *slot = peer + (pb * kMaxCluster + rank) * W + threadIdx.x;
+        if (CL > 1) {
+          if (threadIdx.x == 0) mbar_arrive_expect_tx(xbar, (uint32_t)(CL * W * 4));
+          const uint32_t a = smem_u32(slot), xb = smem_u32(xbar);
+          for (int r = 0; r < CL; ++r)
+            st_async_f32(map_to_cta(a, r), mm, map_to_cta(xb, r));
+        } else {
+          *slot = mm;
+        }
       }
-    }
-    if (CL > 1) cluster_sync();
-    else __syncthreads();
-    m = peer[((l & 1) * kMaxCluster) * W + c];
-    for (int r = 1; r < CL; ++r) m = fmaxf(m, peer[((l & 1) * kMaxCluster + r) * W + c]);
-
-    Level<RD> lv;
-    lv.init(m, alpha);
-    if (rank == 0 && g == 0 && col_ok) scales[((int64_t)b * s + l) * lines + n] = lv.scale;
-
-    const bool upd = l < s - 1;
-#pragma unroll
-    for (int i = 0; i < V / 4; ++i) {
-      Pack<ST, 4> q;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) q.e[u] = quant_step<SK, RD, EXACT>(v[i][u], lv, upd);
-      *reinterpret_cast<Pack<ST, 4> *>(stage + c * PITCH + 4 * (g + G * i) * sizeof(ST)) = q;
-    }
-    __syncthreads();
-    // coalesced 16-byte stores of W K-contiguous rows
-    constexpr int CPL = KC * (int)sizeof(ST) / 16;   // 16-byte chunks per line
-    ST *dst = out + ((int64_t)b * s + l) * lines * (int64_t)ld;
-    for (int id = threadIdx.x; id < W * CPL; id += kColThreads) {
-      int cc = id / CPL, off = id % CPL;
-      int nn = panel * W + cc;
-      int k0 = kbase + off * 16 / (int)sizeof(ST);
-      if (nn < lines && k0 < ld) {
-        uint4 val = *reinterpret_cast<const uint4 *>(stage + cc * PITCH + off * 16);
-        *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(dst + (int64_t)nn * ld + k0)) =
-            val;
+      if (CL > 1) mbar_wait_bounded(xbar, lc & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_CLUSTER);
+      else __syncthreads();
+      ++lc;
+      float mm = peer[(pb * kMaxCluster) * W + c];
+      for (int r = 1; r < CL; ++r) mm = fmaxf(mm, peer[(pb * kMaxCluster + r) * W + c]);
+      return mm;
+    };
+    auto put_scale = [&](int l, float sc) {
+      if (rank == 0 && g == 0 && col_ok) scales[((int64_t)b * s + l) * lines + n] = sc;
+    };
+    Pack<ST, 4> pq;
+    auto emit = [&](int l, int i, ST q) {
+      pq.e[i & 3] = q;
+      if ((i & 3) == 3) {
+        *reinterpret_cast<Pack<ST, 4> *>(outst + c * PITCH + 4 * (g + G * (i >> 2)) * sizeof(ST)) =
+            pq;
+        if (i == V - 1) {
+          // level complete in shared memory: coalesced 16-byte stores
+          __syncthreads();
+          constexpr int CPL = KC * (int)sizeof(ST) / 16;
+          ST *dst = out + ((int64_t)b * s + l) * lines * (int64_t)ld;
+          for (int id = threadIdx.x; id < W * CPL; id += kColCTA) {
+            const int cc = id / CPL, off = id % CPL;
+            const int nn = pn * W + cc;
+            const int k0 = kbase + off * 16 / (int)sizeof(ST);
+            if (nn < lines && k0 < ld)
+              *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(dst + (int64_t)nn * ld + k0)) =
+                  *reinterpret_cast<const uint4 *>(outst + cc * PITCH + off * 16);
+          }
+          __syncthreads();
+        }
       }
-    }
-    __syncthreads();
+    };
+    ll.run(s, alpha, reduce, emit, put_scale);
   }
+  if (CL > 1) cluster_sync();   // no CTA leaves while peers may still address it
 }
 
 // ---------------------------------------------------------------------------
@@ -363,15 +701,34 @@ __global__ void __launch_bounds__(kAnyThreads)
 // ---------------------------------------------------------------------------
 namespace {
 
-template <typename TIn, int SK, bool EXACT, int NC>
+int sm_count_split() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <typename TIn, int SK, bool EXACT, int T, int NC>
 int launch_rows_nc(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K, int ld,
-                   int s, int alpha, void *slices, float *scales, cudaStream_t st, int T) {
-  constexpr int VEC = 16 / (int)sizeof(TIn);
+                   int s, int alpha, void *slices, float *scales, cudaStream_t st, int NS,
+                   int rowp) {
   using ST = typename SliceT<SK>::type;
-  dim3 grid((unsigned)((lines + (kRowThreads / T) - 1) / (kRowThreads / T)), (unsigned)batch);
-  split_rows_kernel<TIn, SK, VEC, NC, EXACT><<<grid, kRowThreads, 0, st>>>(
-      in, sb, sl, lines, K, ld, s, alpha, reinterpret_cast<ST *>(slices), scales, T);
-  return check_cuda(cudaGetLastError(), "split_rows_kernel launch");
+  auto kern = split_rows_tma<TIn, SK, T, NC, EXACT>;
+  const int smem = NS * (kRowCTA / T) * rowp + kRowMaxStages * 8 + 2 * 16 * 4;
+  if (int rc = check_cuda(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          "cudaFuncSetAttribute(split_rows)"))
+    return rc;
+  const int64_t total = batch * (int64_t)lines;
+  const int64_t groups = (total + (kRowCTA / T) - 1) / (kRowCTA / T);
+  const int grid = (int)std::min<int64_t>(groups, (int64_t)sm_count_split());
+  kern<<<grid, kRowCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
+                                    reinterpret_cast<ST *>(slices), scales, NS, rowp);
+  return check_cuda(cudaGetLastError(), "split_rows_tma launch");
 }
 
 template <typename TIn, int SK, bool EXACT>
@@ -379,55 +736,95 @@ int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
   using ST = typename SliceT<SK>::type;
   constexpr int VEC = 16 / (int)sizeof(TIn);
-  // 16-byte vector loads need 16-byte aligned rows
-  const bool vec_ok = ((uintptr_t)in % 16 == 0) && (sl * (int64_t)sizeof(TIn)) % 16 == 0 &&
-                      (sb * (int64_t)sizeof(TIn)) % 16 == 0 && K % VEC == 0 && ld % VEC == 0 &&
-                      ((int64_t)ld * (int64_t)sizeof(ST)) % 16 == 0;
   *done = false;
-  if (!vec_ok) return OZ_OK;
-  // Threads per line T in [32, 256] and chunks per thread NC so that the
-  // coverage T * VEC * NC reaches ld (the tail up to ld is written as zeros).
-  // At most 64 values per thread are held in registers.
-  constexpr int NC_MAX = 64 / VEC;
-  int T = 32, nch = 1;
-  for (;;) {
-    nch = (ld + T * VEC - 1) / (T * VEC);
-    if (nch <= NC_MAX || T == 256) break;
-    T *= 2;
-  }
-  if (nch > NC_MAX) return OZ_OK;  // line too long for the register-resident kernel
-  *done = true;
-  if (nch <= 1) return launch_rows_nc<TIn, SK, EXACT, 1>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  if (nch <= 2) return launch_rows_nc<TIn, SK, EXACT, 2>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  if (nch <= 4) return launch_rows_nc<TIn, SK, EXACT, 4>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  if (nch <= 8) return launch_rows_nc<TIn, SK, EXACT, 8>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  if constexpr (NC_MAX >= 16)
-    if (nch <= 16) return launch_rows_nc<TIn, SK, EXACT, 16>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  if constexpr (NC_MAX >= 32)
-    return launch_rows_nc<TIn, SK, EXACT, (NC_MAX >= 32 ? 32 : 16)>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales, st, T);
-  *done = false;
+  // bulk copies need 16-byte aligned rows whose size is a multiple of 16
+  const bool ok = ((uintptr_t)in % 16 == 0) && (sl * (int64_t)sizeof(TIn)) % 16 == 0 &&
+                  (sb * (int64_t)sizeof(TIn)) % 16 == 0 && K % VEC == 0 && K > 0 &&
+                  ld % VEC == 0 && ((int64_t)ld * (int64_t)sizeof(ST)) % 16 == 0;
+  if (!ok) return OZ_OK;
+  const int rowp = (K * (int)sizeof(TIn) + 127) / 128 * 128;
+  auto go = [&](auto t_tag, auto nc_tag) -> int {
+    constexpr int T = decltype(t_tag)::value, NC = decltype(nc_tag)::value;
+    const int NS = std::min(kRowMaxStages, kRowSmem / ((kRowCTA / T) * rowp));
+    if (NS < 1) return OZ_OK;
+    *done = true;
+    return launch_rows_nc<TIn, SK, EXACT, T, NC>(in, sb, sl, batch, lines, K, ld, s, alpha, slices,
+                                                 scales, st, NS, rowp);
+  };
+  using I = std::integral_constant<int, 0>;
+  (void)sizeof(I);
+  // short rows: 64 threads per row (8 rows per iteration), long rows: 512
+  constexpr int NC_MAX = 32 / VEC;            // at most 32 values per thread
+  const int c64 = (ld + 64 * VEC - 1) / (64 * VEC);
+  const int c512 = (ld + 512 * VEC - 1) / (512 * VEC);
+  if (c64 <= 1) return go(std::integral_constant<int, 64>{}, std::integral_constant<int, 1>{});
+  if (c64 <= 2) return go(std::integral_constant<int, 64>{}, std::integral_constant<int, 2>{});
+  if (c64 <= 4) return go(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
+  if (c512 <= 1) return go(std::integral_constant<int, 512>{}, std::integral_constant<int, 1>{});
+  if (c512 <= 2) return go(std::integral_constant<int, 512>{}, std::integral_constant<int, 2>{});
+  if (c512 <= 4 && NC_MAX >= 4)
+    return go(std::integral_constant<int, 512>{}, std::integral_constant<int, (NC_MAX >= 4 ? 4 : 2)>{});
+  if (c512 <= 8 && NC_MAX >= 8)
+    return go(std::integral_constant<int, 512>{}, std::integral_constant<int, (NC_MAX >= 8 ? 8 : 2)>{});
+  if (c512 <= 16 && NC_MAX >= 16)
+    return go(std::integral_constant<int, 512>{}, std::integral_constant<int, (NC_MAX >= 16 ? 16 : 2)>{});
   return OZ_OK;
 }
 
-template <typename TIn, int SK, bool EXACT, int W, int V>
-int launch_cols_wv(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lines, int K,
-                   int ld, int s, int alpha, void *slices, float *scales, cudaStream_t st,
-                   bool *done) {
+PFN_cuTensorMapEncodeTiled_v12000 split_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+template <typename TIn, int SK, bool EXACT, int V>
+int launch_cols_v(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lines, int K, int ld,
+                  int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
   using ST = typename SliceT<SK>::type;
-  constexpr int G = kColThreads / W, KC = G * V;
+  constexpr int W = 64 / (int)sizeof(TIn);
+  constexpr int G = kColCTA / W, KC = G * V;
+  constexpr int STAGE = KC * 64;
+  constexpr int PITCH = KC * (int)sizeof(ST) + 16;
   const int CL = (ld + KC - 1) / KC;
   if (*done || CL > kMaxCluster) return OZ_OK;
+  const int fixed = W * PITCH + (G * W + 2 * kMaxCluster * W) * 4 + 8 * 5;
+  const int NS = min(4, (kColSmem - fixed) / STAGE);
+  if (NS < 1) return OZ_OK;
   *done = true;
-  const size_t smem = ((size_t)(G * W + 2 * kMaxCluster * W) * 4 + 15) / 16 * 16 +
-                      (size_t)W * (KC * sizeof(ST) + 16);
-  auto kern = split_cols_kernel<TIn, SK, W, V, EXACT>;
+  auto enc = split_encode_fn();
+  if (!enc) return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap map;
+  const CUtensorMapDataType dt = sizeof(TIn) == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64
+                                 : sizeof(TIn) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                    : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  cuuint64_t dims[3] = {(cuuint64_t)lines, (cuuint64_t)K, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(sk * (int64_t)sizeof(TIn)),
+                           (cuuint64_t)(sb * (int64_t)sizeof(TIn))};
+  cuuint32_t box[3] = {(cuuint32_t)W, (cuuint32_t)(KC < 256 ? KC : 256), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(&map, dt, 3, const_cast<TIn *>(in), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled (split) failed (%d)", (int)r);
+  const int smem = NS * STAGE + fixed;
+  auto kern = split_cols_tma<TIn, SK, V, EXACT>;
   if (int rc = check_cuda(
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
           "cudaFuncSetAttribute(split_cols)"))
     return rc;
+  const int64_t work = (int64_t)((lines + W - 1) / W) * batch;
+  const int clusters = (int)std::min<int64_t>(work, (int64_t)std::max(1, sm_count_split() / CL));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(CL * ((lines + W - 1) / W)), (unsigned)batch);
-  cfg.blockDim = dim3(kColThreads);
+  cfg.gridDim = dim3((unsigned)(clusters * CL));
+  cfg.blockDim = dim3(kColCTA);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -438,8 +835,9 @@ int launch_cols_wv(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lin
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   ST *o = reinterpret_cast<ST *>(slices);
-  return check_cuda(cudaLaunchKernelEx(&cfg, kern, in, sb, sk, lines, K, ld, s, alpha, o, scales),
-                    "split_cols_kernel launch");
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, map, lines, (int)batch, K, ld, s, alpha, o,
+                                       scales, NS),
+                    "split_cols_tma launch");
 }
 
 template <typename TIn, int SK, bool EXACT>
@@ -447,21 +845,17 @@ int launch_cols(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lines,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
   using ST = typename SliceT<SK>::type;
   *done = false;
-  if (((int64_t)ld * (int64_t)sizeof(ST)) % 16 != 0) return OZ_OK;
-  // W lines per CTA (row segments of W * sizeof(TIn) bytes), V values per
-  // thread, K rows per CTA = (256 / W) * V, cluster of <= 8 CTAs along K.
-  // The first shape whose cluster covers ld wins: wide segments first, then
-  // short per-thread runs (more CTAs in flight).
-  constexpr int WA = 128 / (int)sizeof(TIn);   // 128-byte row segments
-  constexpr int WB = WA / 2, WC = WA / 4;
+  // TMA: 16-byte aligned base and row pitch; slices rows in 16-byte chunks
+  if (((uintptr_t)in % 16) != 0 || (sk * (int64_t)sizeof(TIn)) % 16 != 0 ||
+      (sb * (int64_t)sizeof(TIn)) % 16 != 0 || ((int64_t)ld * (int64_t)sizeof(ST)) % 16 != 0 ||
+      K <= 0)
+    return OZ_OK;
+  // values per thread: the smallest V whose cluster of <= 8 CTAs covers ld
   int rc = OZ_OK;
-#define OZ_C(W, V)                                                                          \
-  if (rc == OZ_OK && !*done && (W) >= 8)                                                    \
-    rc = launch_cols_wv<TIn, SK, EXACT, ((W) >= 8 ? (W) : 8), V>(in, sb, sk, batch, lines, K, ld, \
-                                                               s, alpha, slices, scales, st, done);
-  OZ_C(WA, 16) OZ_C(WA, 32) OZ_C(WA, 64) OZ_C(WB, 64) OZ_C(WC, 64)
-  if constexpr (sizeof(TIn) == 8) { OZ_C(8, 64) }
-#undef OZ_C
+  rc = launch_cols_v<TIn, SK, EXACT, 4>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales, st, done);
+  if (rc == OZ_OK && !*done) rc = launch_cols_v<TIn, SK, EXACT, 8>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales, st, done);
+  if (rc == OZ_OK && !*done) rc = launch_cols_v<TIn, SK, EXACT, 16>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales, st, done);
+  if (rc == OZ_OK && !*done) rc = launch_cols_v<TIn, SK, EXACT, 32>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales, st, done);
   return rc;
 }
 

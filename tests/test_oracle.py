@@ -81,3 +81,24 @@ def test_bf16_rounding_is_single_rtne():
     assert r[2] == np.float32(1 + 2 ** -6)      # tie to even (up)
     assert r[3] == np.float32(-0.30078125)
     assert np.isinf(r[4])
+
+
+def test_ceil_log2_table_matches_oracle():
+    """The device's per-binade threshold table (generated header) gives the
+    oracle's ceil(fl32(log2 m)) for every normal binade."""
+    import os
+    import re
+
+    hdr = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                       "ozaki_triton_b200", "csrc", "oz_log2_table.h")
+    txt = open(hdr).read()
+    thr = np.array([int(v) for v in re.findall(r"-?\d+", txt.split("{", 1)[1])][:256])
+    rng = np.random.default_rng(1)
+    bits = rng.integers(0x00800000, 0x7F7FFFFF, 200_000).astype(np.uint32)
+    k = np.arange(0, 200, dtype=np.uint32)
+    edge = ((np.arange(1, 255, dtype=np.uint32)[:, None] << 23) | k[None, :]).ravel()
+    bits = np.concatenate([bits, edge])
+    m = bits.view(np.float32)
+    b = (bits >> 23).astype(np.int64)
+    c = b - 127 + ((bits & 0x7FFFFF).astype(np.int64) >= thr[b])
+    assert np.array_equal(c, oracle.ceil_log2_f32(m))
