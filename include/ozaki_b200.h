@@ -85,6 +85,29 @@ int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t
              void *slices, int64_t ld, float *scales, void *stream);
 
 /*
+ * Scratch bytes that oz_split_ex can use for this input layout (0 when none
+ * helps).  When the lines are contiguous (stride_line == 1: the columns of a
+ * row-major B) oz_split_ex first transposes them into the workspace
+ * ((batch, lines, k padded to 16 bytes), input dtype) so that each line is
+ * read as one contiguous row by the row kernel.
+ */
+int64_t oz_split_workspace_bytes(int in_dtype, int64_t batch, int64_t lines, int64_t k,
+                                 int64_t stride_line, int64_t stride_k);
+
+/*
+ * oz_split with caller-provided scratch memory (device, 16-byte aligned).
+ * Same results as oz_split; with workspace_bytes >= oz_split_workspace_bytes()
+ * the column layout goes through the transpose described above, otherwise
+ * it behaves exactly like oz_split.  Also replaces split_matrix
+ * (ozaki_triton.py:214-256), whose fp32 residual buffer is a workspace too.
+ */
+int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+                int64_t stride_b, int64_t stride_line, int64_t stride_k,
+                int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
+                void *slices, int64_t ld, float *scales, void *workspace,
+                int64_t workspace_bytes, void *stream);
+
+/*
  * Fused cross-GEMM over all slice pairs.
  * Replaces cross_gemm (ozaki_triton.py:455-498) and cross_gemm_kernel
  * (ozaki_triton.py:305-452):

@@ -30,6 +30,9 @@ SIGNATURES = {
     "oz_slice_row_bytes": (_i64, [_i64, _int]),
     "oz_split": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _int, _int,
                         _vp, _i64, _vp, _vp]),
+    "oz_split_workspace_bytes": (_i64, [_int, _i64, _i64, _i64, _i64, _i64]),
+    "oz_split_ex": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _int, _int,
+                           _vp, _i64, _vp, _vp, _i64, _vp]),
     "oz_cross_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int, _int,
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),

@@ -121,10 +121,14 @@ def _split_lines(x3: torch.Tensor, stride_line: int, stride_k: int, lines: int, 
     if batch == 0 or lines == 0:
         return slices, scales
     lib = _lib.load()
-    _lib.check(lib.oz_split(
-        x3.data_ptr(), _OZ_DTYPE[x3.dtype], batch, lines, k,
+    code = _OZ_DTYPE[x3.dtype]
+    ws_bytes = lib.oz_split_workspace_bytes(code, batch, lines, k, stride_line, stride_k)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x3.device) if ws_bytes > 0 else None
+    _lib.check(lib.oz_split_ex(
+        x3.data_ptr(), code, batch, lines, k,
         x3.stride(0), stride_line, stride_k, num_splits, alpha, _OZ_DTYPE[slice_dtype], mode,
-        slices.data_ptr(), ld, scales.data_ptr(), _stream_ptr(x3.device)))
+        slices.data_ptr(), ld, scales.data_ptr(), ws.data_ptr() if ws is not None else None,
+        ws_bytes, _stream_ptr(x3.device)))
     return slices, scales
 
 

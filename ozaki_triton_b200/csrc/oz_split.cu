@@ -697,6 +697,33 @@ __global__ void __launch_bounds__(kAnyThreads)
 }
 
 // ---------------------------------------------------------------------------
+// transpose of contiguous lines into a K-contiguous workspace
+// ---------------------------------------------------------------------------
+// ws[(b * lines + n) * kp + k] = in[b * stride_b + k * stride_k + n] for k < K,
+// 0 for K <= k < kp.  32 x 32 tiles through padded shared memory; reads and
+// writes are coalesced along n and k respectively.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    transpose_lines(const T *__restrict__ in, int64_t stride_b, int64_t stride_k, int lines, int K,
+                    int kp, T *__restrict__ ws) {
+  __shared__ T tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32, b = blockIdx.z;
+  const T *src = in + (int64_t)b * stride_b;
+#pragma unroll
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int k = k0 + r, n = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (k < K && n < lines) ? src[(int64_t)k * stride_k + n] : (T)0.0f;
+  }
+  __syncthreads();
+  T *dst = ws + (int64_t)b * lines * kp;
+#pragma unroll
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int n = n0 + r, k = k0 + threadIdx.x;
+    if (n < lines && k < kp) dst[(int64_t)n * kp + k] = tile[threadIdx.x][r];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------
 namespace {
@@ -912,11 +939,35 @@ extern "C" int64_t oz_slice_row_bytes(int64_t k, int slice_dtype) {
   return (bytes + 127) / 128 * 128;
 }
 
-extern "C" int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
-                        int64_t stride_b, int64_t stride_line, int64_t stride_k,
-                        int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
-                        void *slices, int64_t ld, float *scales, void *stream) {
-  using namespace oz;
+namespace oz {
+namespace {
+
+// padded row length (elements) of the transposed workspace: 16-byte rows
+int64_t ws_row(int in_dtype, int64_t k) {
+  const int es = dtype_size(in_dtype);
+  const int64_t vec = 16 / es;
+  return (k + vec - 1) / vec * vec;
+}
+
+bool ws_applies(int in_dtype, int64_t lines, int64_t k, int64_t stride_line, int64_t stride_k) {
+  return stride_line == 1 && stride_k != 1 && k > 0 && lines > 0 &&
+         (in_dtype == OZ_F64 || in_dtype == OZ_F32 || in_dtype == OZ_F16 || in_dtype == OZ_BF16);
+}
+
+template <typename T>
+int transpose_into(const void *in, int64_t batch, int64_t lines, int64_t k, int64_t sb,
+                   int64_t sk, int64_t kp, void *ws, cudaStream_t st) {
+  dim3 grid((unsigned)((lines + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)batch);
+  transpose_lines<T><<<grid, dim3(32, 8), 0, st>>>(reinterpret_cast<const T *>(in), sb, sk,
+                                                   (int)lines, (int)k, (int)kp,
+                                                   reinterpret_cast<T *>(ws));
+  return check_cuda(cudaGetLastError(), "transpose_lines launch");
+}
+
+int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+               int64_t stride_b, int64_t stride_line, int64_t stride_k, int32_t num_splits,
+               int32_t alpha, int slice_dtype, int residual_mode, void *slices, int64_t ld,
+               float *scales, void *workspace, int64_t workspace_bytes, void *stream) {
   if (num_splits < 1 || num_splits > kMaxSplits)
     return set_error(OZ_ERR_INVALID, "num_splits must be in [1, %d], got %d", kMaxSplits,
                      num_splits);
@@ -927,16 +978,39 @@ extern "C" int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lin
   if (slice_dtype != OZ_I8 && slice_dtype != OZ_F16 && slice_dtype != OZ_BF16 &&
       slice_dtype != OZ_F32)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported slice dtype %d", slice_dtype);
+  if (in_dtype != OZ_F64 && in_dtype != OZ_F32 && in_dtype != OZ_F16 && in_dtype != OZ_BF16)
+    return set_error(OZ_ERR_UNSUPPORTED, "unsupported input dtype %d", in_dtype);
   if (residual_mode != OZ_RESIDUAL_COMPAT && residual_mode != OZ_RESIDUAL_EXACT)
     return set_error(OZ_ERR_INVALID, "unknown residual mode %d", residual_mode);
   if (ld < k) return set_error(OZ_ERR_INVALID, "slice row pitch %lld < k %lld", (long long)ld,
                                (long long)k);
   if (batch == 0 || lines == 0) return OZ_OK;
   if (!in || !slices || !scales) return set_error(OZ_ERR_INVALID, "null pointer");
-  if (lines > INT32_MAX || ld > INT32_MAX || batch > 65535)
+  if (lines > INT32_MAX || ld > INT32_MAX || k > INT32_MAX || batch > 65535)
     return set_error(OZ_ERR_INVALID, "size out of range (lines=%lld ld=%lld batch=%lld)",
                      (long long)lines, (long long)ld, (long long)batch);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  // contiguous lines (columns of a row-major B): transpose into the
+  // workspace, then split the transposed rows with the row kernel
+  if (workspace && ws_applies(in_dtype, lines, k, stride_line, stride_k)) {
+    const int64_t kp = ws_row(in_dtype, k);
+    const int64_t need = batch * lines * kp * dtype_size(in_dtype);
+    if (workspace_bytes >= need && kp <= ld && (uintptr_t)workspace % 16 == 0) {
+      int rc;
+      switch (in_dtype) {
+        case OZ_F64: rc = transpose_into<double>(in, batch, lines, k, stride_b, stride_k, kp, workspace, st); break;
+        case OZ_F32: rc = transpose_into<float>(in, batch, lines, k, stride_b, stride_k, kp, workspace, st); break;
+        default: rc = transpose_into<unsigned short>(in, batch, lines, k, stride_b, stride_k, kp, workspace, st); break;
+      }
+      if (rc) return rc;
+      in = workspace;
+      stride_b = lines * kp;
+      stride_line = kp;
+      stride_k = 1;
+      k = kp;
+    }
+  }
   switch (in_dtype) {
     case OZ_F64:
       return dispatch_slice<double>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
@@ -947,10 +1021,37 @@ extern "C" int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lin
     case OZ_F16:
       return dispatch_slice<__half>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
                                     stride_line, stride_k, num_splits, alpha, slices, ld, scales, st);
-    case OZ_BF16:
+    default:
       return dispatch_slice<__nv_bfloat16>(slice_dtype, residual_mode, in, batch, lines, k,
                                            stride_b, stride_line, stride_k, num_splits, alpha,
                                            slices, ld, scales, st);
   }
-  return set_error(OZ_ERR_UNSUPPORTED, "unsupported input dtype %d", in_dtype);
+}
+
+}  // namespace
+}  // namespace oz
+
+extern "C" int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+                        int64_t stride_b, int64_t stride_line, int64_t stride_k,
+                        int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
+                        void *slices, int64_t ld, float *scales, void *stream) {
+  return oz::split_impl(in, in_dtype, batch, lines, k, stride_b, stride_line, stride_k,
+                        num_splits, alpha, slice_dtype, residual_mode, slices, ld, scales, nullptr,
+                        0, stream);
+}
+
+extern "C" int64_t oz_split_workspace_bytes(int in_dtype, int64_t batch, int64_t lines,
+                                            int64_t k, int64_t stride_line, int64_t stride_k) {
+  if (!oz::ws_applies(in_dtype, lines, k, stride_line, stride_k) || batch <= 0) return 0;
+  return batch * lines * oz::ws_row(in_dtype, k) * oz::dtype_size(in_dtype);
+}
+
+extern "C" int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+                           int64_t stride_b, int64_t stride_line, int64_t stride_k,
+                           int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
+                           void *slices, int64_t ld, float *scales, void *workspace,
+                           int64_t workspace_bytes, void *stream) {
+  return oz::split_impl(in, in_dtype, batch, lines, k, stride_b, stride_line, stride_k,
+                        num_splits, alpha, slice_dtype, residual_mode, slices, ld, scales,
+                        workspace, workspace_bytes, stream);
 }

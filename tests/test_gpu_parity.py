@@ -312,3 +312,46 @@ def test_gemm_tile_configs_bit_identical(tile, s, monkeypatch):
     want = oracle.ozaki_matmul(a, b, s, "int8", "fp64")
     assert same_bits(host(c), want)
     assert oz.device_status() == 0
+
+
+@pytest.mark.parametrize("use_ws", [False, True])
+@pytest.mark.parametrize("ik,sk,K", [("fp64", "int8", 8192), ("fp64", "int8", 300),
+                                     ("fp32", "fp16", 1000), ("bf16", "int8", 2048),
+                                     ("fp64", "fp32", 77)])
+def test_split_columns_c_abi_workspace_and_cluster(use_ws, ik, sk, K):
+    """Columns of a row-major matrix through the C ABI: oz_split (cluster
+    kernel, no scratch) and oz_split_ex with the transpose workspace give the
+    same bits as the oracle."""
+    from ozaki_triton_b200 import _lib
+    from ozaki_triton_b200.api import _OZ_DTYPE
+    rng = np.random.default_rng(K + len(ik))
+    N = 70
+    b = rand_lines(rng, (2, N, K), ik)
+    bd = to_dev(np.ascontiguousarray(np.swapaxes(b, -1, -2)), ik)     # (2, K, N) row-major
+    lines_np = np.swapaxes(host(bd).astype(np.float64 if ik == "fp64" else np.float32), -1, -2)
+    s = 3
+    alpha = oz.compute_split_bits(K, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    ld = oz.slice_row_elems(K, TDT[sk])
+    sl = torch.empty((2, s, N, ld), dtype=TDT[sk], device=DEV)
+    sc = torch.empty((2, s, N), dtype=torch.float32, device=DEV)
+    lib = _lib.load()
+    code = _OZ_DTYPE[TDT[ik]]
+    st = torch.cuda.current_stream().cuda_stream
+    if use_ws:
+        nbytes = lib.oz_split_workspace_bytes(code, 2, N, K, 1, N)
+        assert nbytes > 0
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+        rc = lib.oz_split_ex(bd.data_ptr(), code, 2, N, K, K * N, 1, N, s, alpha,
+                             _OZ_DTYPE[TDT[sk]], 0, sl.data_ptr(), ld, sc.data_ptr(),
+                             ws.data_ptr(), nbytes, st)
+    else:
+        rc = lib.oz_split(bd.data_ptr(), code, 2, N, K, K * N, 1, N, s, alpha,
+                          _OZ_DTYPE[TDT[sk]], 0, sl.data_ptr(), ld, sc.data_ptr(), st)
+    _lib.check(rc)
+    rsl, rsc = oracle.split_lines(lines_np, s, alpha, sk, ik)
+    torch.cuda.synchronize()
+    assert same_bits(host(sc), rsc)
+    got = host(sl[..., :K])
+    assert same_bits(got, rsl if sk == "int8" else rsl.astype(np.float32))
+    # padding beyond K is zero
+    assert not host(sl[..., K:]).any()
