@@ -108,6 +108,34 @@ int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t lines, int6
                 int64_t workspace_bytes, void *stream);
 
 /*
+ * oz_split without any allocation, for callers that cannot call cudaMalloc:
+ * code that reaches the library through a foreign-function binding holding
+ * only the raw device pointers it was handed (no device allocator of its
+ * own), and latency-critical loops in which cudaMalloc's implicit
+ * device-wide synchronisation is not acceptable.  (No counterpart in the
+ * reference, which allocates its residual buffer on every call.)
+ *
+ * Identical results to oz_split_ex.  The scratch that oz_split_ex takes from
+ * the caller (column layouts only, size oz_split_workspace_bytes()) comes
+ * from a fixed array of oz_split_noalloc_max_bytes() bytes (32 MiB) that the
+ * library keeps in device memory of every GPU it is loaded on, until the
+ * process exits.  Inputs needing more scratch are rejected with
+ * OZ_ERR_INVALID before any launch.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (different streams, or different host threads on one device) race
+ * and corrupt each other's slices; serialise them.  Nothing in the array has
+ * to start at zero: every byte a call reads was written earlier in that call.
+ */
+int oz_split_noalloc(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
+                     int64_t stride_b, int64_t stride_line, int64_t stride_k,
+                     int32_t num_splits, int32_t alpha, int slice_dtype, int residual_mode,
+                     void *slices, int64_t ld, float *scales, void *stream);
+
+/* Size in bytes of oz_split_noalloc's fixed device scratch array. */
+int64_t oz_split_noalloc_max_bytes(void);
+
+/*
  * Fused cross-GEMM over all slice pairs.
  * Replaces cross_gemm (ozaki_triton.py:455-498) and cross_gemm_kernel
  * (ozaki_triton.py:305-452):

@@ -33,6 +33,9 @@ SIGNATURES = {
     "oz_split_workspace_bytes": (_i64, [_int, _i64, _i64, _i64, _i64, _i64]),
     "oz_split_ex": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _int, _int,
                            _vp, _i64, _vp, _vp, _i64, _vp]),
+    "oz_split_noalloc": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _int,
+                                _int, _vp, _i64, _vp, _vp]),
+    "oz_split_noalloc_max_bytes": (_i64, []),
     "oz_cross_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int, _int,
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 #include <type_traits>
 #include <cudaTypedefs.h>
 
@@ -1054,4 +1055,67 @@ extern "C" int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t 
   return oz::split_impl(in, in_dtype, batch, lines, k, stride_b, stride_line, stride_k,
                         num_splits, alpha, slice_dtype, residual_mode, slices, ld, scales,
                         workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// allocation-free variant of oz_split_ex
+// ---------------------------------------------------------------------------
+// Scratch for the column transpose of oz_split_noalloc: a fixed array in
+// device memory, present on every GPU that loads the library until the
+// process exits.  Host code must not hand the symbol itself to a kernel (on
+// the host it is only a stand-in); the device address is looked up once per
+// device with cudaGetSymbolAddress.
+namespace oz {
+constexpr int64_t kNoAllocScratchBytes = 32ll << 20;   // 32 MiB
+}
+static __device__ __align__(256) unsigned char g_split_scratch[oz::kNoAllocScratchBytes];
+
+namespace oz {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_ptr[kMaxDevices] = {};
+
+// device address of g_split_scratch on the current device (looked up on the
+// first call for that device)
+int scratch_address(void **out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(OZ_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_split_scratch),
+                            "cudaGetSymbolAddress(g_split_scratch)"))
+      return rc;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return OZ_OK;
+}
+}  // namespace
+}  // namespace oz
+
+extern "C" int64_t oz_split_noalloc_max_bytes(void) { return oz::kNoAllocScratchBytes; }
+
+extern "C" int oz_split_noalloc(const void *in, int in_dtype, int64_t batch, int64_t lines,
+                                int64_t k, int64_t stride_b, int64_t stride_line, int64_t stride_k,
+                                int32_t num_splits, int32_t alpha, int slice_dtype,
+                                int residual_mode, void *slices, int64_t ld, float *scales,
+                                void *stream) {
+  using namespace oz;
+  const int64_t need =
+      oz_split_workspace_bytes(in_dtype, batch, lines, k, stride_line, stride_k);
+  if (need > kNoAllocScratchBytes)
+    return set_error(OZ_ERR_INVALID,
+                     "oz_split_noalloc: this input needs %lld bytes of scratch, more than the "
+                     "library's fixed %lld-byte device array; use oz_split_ex with a workspace",
+                     (long long)need, (long long)kNoAllocScratchBytes);
+  void *scratch = nullptr;
+  if (need > 0)
+    if (int rc = scratch_address(&scratch)) return rc;
+  // the transpose writes every workspace byte the split then reads (zero
+  // padding included), so the array needs no clearing between calls
+  return split_impl(in, in_dtype, batch, lines, k, stride_b, stride_line, stride_k, num_splits,
+                    alpha, slice_dtype, residual_mode, slices, ld, scales, scratch, need, stream);
 }
