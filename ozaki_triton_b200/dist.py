@@ -1,0 +1,180 @@
+"""Multi-GPU Ozaki GEMM: one process per GPU over ``torch.distributed``.
+
+The reference runs one GPU per independent problem only (its harness pools
+processes, ``test.py:77-81``); it has no sharded path.  Two partitions are
+provided here, both without a reduction collective because every A row and
+every B column is split independently (per-row / per-column scales), so a
+shard's slices are bit-identical to the corresponding rows of the global
+split:
+
+* ``ozaki_matmul_mrows``: A sharded by row blocks; B lives on one root rank,
+  which splits it once and broadcasts its slices and scales (for int8 slices
+  half the bytes of the fp64 B); every rank computes its rows of C.  The
+  broadcast runs while each rank splits its own A rows.
+* ``ozaki_matmul_batches``: the broadcast batch of a batched matmul is cut in
+  contiguous ranges of output batches; each rank computes its range from the
+  operand members that range references (no exchange at all).
+
+The device work goes through a ``Backend`` (the CUDA library by default); the
+CPU tests plug in the oracle to check the partitioning and the collective
+protocol on ``gloo`` ranks.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .api import (
+    MAX_SPLITS,
+    SLICE_DTYPE_INFO,
+    _OZ_DTYPE,
+    _batch_index,
+    _residual_mode,
+    _split_lines,
+    compute_split_bits,
+    select_dot_accum_dtype,
+)
+
+
+def block_range(total: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous, balanced [start, stop) of ``total`` units for ``rank``."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class Backend:
+    """Device compute used by the sharded drivers (the CUDA library)."""
+
+    def split(self, x3: torch.Tensor, stride_line: int, stride_k: int, lines: int, k: int,
+              num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int):
+        return _split_lines(x3, stride_line, stride_k, lines, k, num_splits, alpha,
+                            slice_dtype, mode)
+
+    def gemm(self, a_sl, b_sl, a_sc, b_sc, batch: int, m: int, n: int, k: int, num_splits: int,
+             out_dtype: torch.dtype, skip_tail: bool, a_idx=None, b_idx=None) -> torch.Tensor:
+        c = torch.empty((batch, m, n), dtype=out_dtype, device=a_sl.device)
+        if batch == 0 or m == 0 or n == 0:
+            return c
+        _lib.check(_lib.load().oz_cross_gemm(
+            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), batch, m, n, k,
+            a_sl.shape[-1], num_splits, _OZ_DTYPE[a_sl.dtype], _OZ_DTYPE[out_dtype],
+            a_idx.data_ptr() if a_idx is not None else None,
+            b_idx.data_ptr() if b_idx is not None else None, a_sl.shape[0], b_sl.shape[0],
+            c.data_ptr(), n, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+            torch.cuda.current_stream(a_sl.device).cuda_stream))
+        return c
+
+
+def _check_args(dtype, num_splits, slice_dtype):
+    assert slice_dtype in SLICE_DTYPE_INFO, f"unsupported slice dtype: {slice_dtype}"
+    assert 1 <= num_splits <= MAX_SPLITS, f"num_splits must be in [1, {MAX_SPLITS}]"
+    assert dtype in (torch.float64, torch.float32, torch.float16, torch.bfloat16), \
+        f"unsupported input dtype: {dtype}"
+
+
+def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_splits: int = 3,
+                       slice_dtype: torch.dtype = torch.float16, *, root: int = 0,
+                       group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
+                       backend: Optional[Backend] = None) -> torch.Tensor:
+    """C_local = A_local @ B, A sharded by rows, B on ``root`` only.
+
+    Every rank passes its own rows of A (M_local, K) (M_local may differ per
+    rank, including 0); the root passes B (K, N), the others may pass None.
+    Returns this rank's rows of C (M_local, N) in the input dtype, equal bit
+    for bit to the same rows of the single-GPU ``ozaki_matmul``.
+    """
+    backend = backend or Backend()
+    dev = A_local.device
+    _check_args(A_local.dtype, num_splits, slice_dtype)
+    m_loc, k = A_local.shape
+    rank = dist.get_rank(group)
+    # the root announces N (and checks K); every rank takes the same steps
+    shape = torch.tensor([B.shape[0], B.shape[1]] if rank == root else [0, 0],
+                         dtype=torch.int64, device=dev)
+    dist.broadcast(shape, src=root, group=group)
+    k_b, n = int(shape[0]), int(shape[1])
+    assert k_b == k, f"contraction dim mismatch: A K={k}, B K={k_b}"
+    alpha = compute_split_bits(k, slice_dtype=slice_dtype,
+                               dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
+    mode = _residual_mode(residual, num_splits, A_local.dtype)
+    ld = _lib_row(k, slice_dtype)
+    if rank == root:
+        B3 = B.reshape(1, k, n)
+        b_sl, b_sc = backend.split(B3, B3.stride(2), B3.stride(1), n, k, num_splits, alpha,
+                                   slice_dtype, mode)
+    else:
+        b_sl = torch.empty((1, num_splits, n, ld), dtype=slice_dtype, device=dev)
+        b_sc = torch.empty((1, num_splits, n), dtype=torch.float32, device=dev)
+    # broadcast B's slices while this rank splits its rows of A
+    w1 = dist.broadcast(b_sl, src=root, group=group, async_op=True)
+    w2 = dist.broadcast(b_sc, src=root, group=group, async_op=True)
+    A3 = A_local.reshape(1, m_loc, k)
+    a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
+                               slice_dtype, mode)
+    w1.wait()
+    w2.wait()
+    c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
+                     skip_tail)
+    return c.reshape(m_loc, n)
+
+
+def ozaki_matmul_batches(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
+                         slice_dtype: torch.dtype = torch.float16, *, group=None,
+                         skip_tail: bool = False, residual: Optional[str] = "auto",
+                         backend: Optional[Backend] = None) -> Tuple[torch.Tensor, int, int]:
+    """This rank's contiguous range of the broadcast batch of A @ B.
+
+    A: (..., M, K), B: (..., K, N) on every rank (torch.matmul broadcasting).
+    Returns (C_range (n_b, M, N), start, stop): output batches [start, stop)
+    of the flattened broadcast batch.  Only the A and B members the range
+    references are split.
+    """
+    backend = backend or Backend()
+    _check_args(A.dtype, num_splits, slice_dtype)
+    assert A.dtype == B.dtype
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    M, K = A.shape[-2:]
+    K2, N = B.shape[-2:]
+    assert K == K2
+    a_batch, b_batch = tuple(A.shape[:-2]), tuple(B.shape[:-2])
+    full = tuple(torch.broadcast_shapes(a_batch, b_batch))
+    bn = math.prod(full)
+    start, stop = block_range(bn, world, rank)
+    alpha = compute_split_bits(K, slice_dtype=slice_dtype,
+                               dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
+    mode = _residual_mode(residual, num_splits, A.dtype)
+    a_all = _batch_index(a_batch, full, "cpu")
+    b_all = _batch_index(b_batch, full, "cpu")
+    a_all = torch.arange(bn, dtype=torch.int32) if a_all is None else a_all
+    b_all = torch.arange(bn, dtype=torch.int32) if b_all is None else b_all
+    a_need = torch.unique(a_all[start:stop]) if stop > start else a_all[:0]
+    b_need = torch.unique(b_all[start:stop]) if stop > start else b_all[:0]
+    A3 = A.reshape(math.prod(a_batch), M, K)[a_need.long().to(A.device)]
+    B3 = B.reshape(math.prod(b_batch), K, N)[b_need.long().to(B.device)]
+    if stop == start:
+        return torch.empty((0, M, N), dtype=A.dtype, device=A.device), start, stop
+    # renumber the members this range uses
+    a_map = {int(v): i for i, v in enumerate(a_need.tolist())}
+    b_map = {int(v): i for i, v in enumerate(b_need.tolist())}
+    a_idx = torch.tensor([a_map[int(v)] for v in a_all[start:stop].tolist()], dtype=torch.int32,
+                         device=A.device)
+    b_idx = torch.tensor([b_map[int(v)] for v in b_all[start:stop].tolist()], dtype=torch.int32,
+                         device=A.device)
+    b_sl, b_sc = backend.split(B3, B3.stride(2), B3.stride(1), N, K, num_splits, alpha,
+                               slice_dtype, mode)
+    a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), M, K, num_splits, alpha,
+                               slice_dtype, mode)
+    c = backend.gemm(a_sl, b_sl, a_sc, b_sc, stop - start, M, N, K, num_splits, A.dtype,
+                     skip_tail, a_idx, b_idx)
+    return c, start, stop
+
+
+def _lib_row(k: int, slice_dtype: torch.dtype) -> int:
+    es = torch.empty((), dtype=slice_dtype).element_size()
+    return ((k * es + 127) // 128 * 128) // es if k > 0 else 0

@@ -1,0 +1,173 @@
+"""Host-side multi-rank logic of ozaki_triton_b200.dist on CPU gloo ranks.
+
+The device compute is replaced by the CPU oracle (a Backend with the same
+interface), so these tests check the partitioning, the B broadcast protocol,
+the batch-range bookkeeping and failure behaviour -- not the kernels (the
+GPU tests do that).
+"""
+
+import os
+import socket
+import time
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from ozaki_triton_b200 import dist as ozd
+
+KIND = {torch.float64: "fp64", torch.float32: "fp32", torch.float16: "fp16", torch.int8: "int8"}
+
+
+class OracleBackend:
+    """CPU stand-in for the CUDA library with the library's slice layout."""
+
+    def __init__(self, residual="compat"):
+        self.residual = residual
+
+    def split(self, x3, stride_line, stride_k, lines, k, s, alpha, slice_dtype, mode):
+        x = torch.as_strided(x3, (x3.shape[0], lines, k), (x3.stride(0), stride_line, stride_k))
+        sl, sc = oracle.split_lines(x.numpy(), s, alpha, KIND[slice_dtype], KIND[x3.dtype],
+                                    residual="compat" if mode == 0 else "exact")
+        ld = ozd._lib_row(k, slice_dtype)
+        out = torch.zeros((x3.shape[0], s, lines, ld), dtype=slice_dtype)
+        out[..., :k] = torch.from_numpy(sl.astype(np.float32) if slice_dtype != torch.int8 else sl
+                                        ).to(slice_dtype)
+        return out, torch.from_numpy(sc)
+
+    def gemm(self, a_sl, b_sl, a_sc, b_sc, batch, m, n, k, s, out_dtype, skip_tail,
+             a_idx=None, b_idx=None):
+        ai = a_idx.long() if a_idx is not None else torch.arange(batch)
+        bi = b_idx.long() if b_idx is not None else torch.arange(batch)
+        a = a_sl[ai, ..., :k].numpy()
+        b = b_sl[bi, ..., :k].numpy()
+        c = oracle.cross_gemm(a, b, a_sc[ai].numpy(), b_sc[bi].numpy(), KIND[a_sl.dtype],
+                              KIND[out_dtype], skip_tail)
+        return torch.from_numpy(np.ascontiguousarray(c))
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, out_dir):
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=timedelta(seconds=20))
+        case(rank, world, out_dir)
+        dist.destroy_process_group()
+    except BaseException:  # report to the parent
+        with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as fh:
+            fh.write(traceback.format_exc())
+        raise
+
+
+def run_ranks(case, world, tmp_path):
+    port = free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    return [p.exitcode for p in procs]
+
+
+def law(g, shape):
+    return (torch.rand(shape, generator=g, dtype=torch.float64) - 0.5) * torch.exp(
+        torch.randn(shape, generator=g, dtype=torch.float64))
+
+
+def case_mrows(rank, world, out_dir):
+    g = torch.Generator().manual_seed(5)
+    A = law(g, (37, 64))
+    B = law(g, (64, 23))
+    lo, hi = ozd.block_range(37, world, rank)
+    c = ozd.ozaki_matmul_mrows(A[lo:hi], B if rank == 0 else None, 4, torch.int8,
+                               backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"c{rank}.npy"), c.numpy())
+
+
+def case_batches(rank, world, out_dir):
+    g = torch.Generator().manual_seed(6)
+    A = law(g, (4, 1, 8, 16))
+    B = law(g, (1, 3, 16, 5))
+    c, lo, hi = ozd.ozaki_matmul_batches(A, B, 3, torch.float16, backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"c{rank}.npy"), c.numpy())
+    np.save(os.path.join(out_dir, f"r{rank}.npy"), np.array([lo, hi]))
+
+
+def case_root_fails(rank, world, out_dir):
+    """The root dies before the broadcast: the other rank's collective must end
+    with an error within the process-group timeout, not hang."""
+    g = torch.Generator().manual_seed(7)
+    A = law(g, (8, 16))
+    B = law(g, (16, 4))
+    if rank == 0:
+        raise RuntimeError("injected failure on the root before the broadcast")
+    t0 = time.time()
+    try:
+        ozd.ozaki_matmul_mrows(A, None, 2, torch.int8, backend=OracleBackend())
+    except Exception as e:  # noqa: BLE001
+        with open(os.path.join(out_dir, "peer_error.txt"), "w") as fh:
+            fh.write(f"{type(e).__name__} after {time.time() - t0:.1f}s: {e}")
+        return
+    with open(os.path.join(out_dir, "peer_error.txt"), "w") as fh:
+        fh.write("NO ERROR")
+
+
+def test_block_range_covers_everything():
+    for total in [0, 1, 7, 128, 8192, 8193]:
+        for world in [1, 2, 3, 4, 8]:
+            ranges = [ozd.block_range(total, world, r) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == total
+            for (a, b), (c, d) in zip(ranges, ranges[1:]):
+                assert b == c and b >= a
+            sizes = [b - a for a, b in ranges]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_mrows_two_ranks_bit_identical(tmp_path):
+    codes = run_ranks(case_mrows, 2, tmp_path)
+    assert codes == [0, 0], [open(p).read() for p in tmp_path.glob("err*.txt")]
+    c = np.concatenate([np.load(tmp_path / f"c{r}.npy") for r in range(2)])
+    g = torch.Generator().manual_seed(5)
+    A = law(g, (37, 64))
+    B = law(g, (64, 23))
+    want = oracle.ozaki_matmul(A.numpy(), B.numpy(), 4, "int8", "fp64")
+    assert np.array_equal(c, want)
+
+
+def test_batches_two_ranks_cover_the_broadcast(tmp_path):
+    codes = run_ranks(case_batches, 2, tmp_path)
+    assert codes == [0, 0], [open(p).read() for p in tmp_path.glob("err*.txt")]
+    parts = [np.load(tmp_path / f"c{r}.npy") for r in range(2)]
+    ranges = [tuple(np.load(tmp_path / f"r{r}.npy")) for r in range(2)]
+    assert ranges[0][0] == 0 and ranges[0][1] == ranges[1][0] and ranges[1][1] == 12
+    g = torch.Generator().manual_seed(6)
+    A = law(g, (4, 1, 8, 16))
+    B = law(g, (1, 3, 16, 5))
+    want = oracle.ozaki_matmul(A.numpy(), B.numpy(), 3, "fp16", "fp64").reshape(12, 8, 5)
+    got = np.concatenate(parts)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err < 1e-12
+
+
+def test_root_failure_is_reported_not_hung(tmp_path):
+    t0 = time.time()
+    codes = run_ranks(case_root_fails, 2, tmp_path)
+    assert codes[0] != 0                       # the injected failure
+    msg = (tmp_path / "peer_error.txt").read_text()
+    assert msg != "NO ERROR", msg              # the peer saw an error ...
+    assert time.time() - t0 < 110              # ... within the timeout, no hang
