@@ -197,6 +197,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-dgemm", action="store_true")
+    ap.add_argument("--root-discount", type=int, default=768,
+                    help="multi-GPU: rows of A moved off rank 0, which also splits B")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="multi-GPU: column blocks B is broadcast in (0 = by GPU count)")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, DGEMM or CPU legs): the ncu command line")
     args = ap.parse_args()

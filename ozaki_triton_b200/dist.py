@@ -57,16 +57,20 @@ class Backend:
                             slice_dtype, mode)
 
     def gemm(self, a_sl, b_sl, a_sc, b_sc, batch: int, m: int, n: int, k: int, num_splits: int,
-             out_dtype: torch.dtype, skip_tail: bool, a_idx=None, b_idx=None) -> torch.Tensor:
-        c = torch.empty((batch, m, n), dtype=out_dtype, device=a_sl.device)
+             out_dtype: torch.dtype, skip_tail: bool, a_idx=None, b_idx=None,
+             out: Optional[torch.Tensor] = None, col0: int = 0) -> torch.Tensor:
+        """C (batch, m, n); with ``out`` (batch, m, N_total) the result is written
+        into its columns [col0, col0 + n) instead."""
+        c = torch.empty((batch, m, n), dtype=out_dtype, device=a_sl.device) if out is None else out
         if batch == 0 or m == 0 or n == 0:
             return c
+        ptr = c.data_ptr() + col0 * c.element_size()
         _lib.check(_lib.load().oz_cross_gemm(
             a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), batch, m, n, k,
             a_sl.shape[-1], num_splits, _OZ_DTYPE[a_sl.dtype], _OZ_DTYPE[out_dtype],
             a_idx.data_ptr() if a_idx is not None else None,
             b_idx.data_ptr() if b_idx is not None else None, a_sl.shape[0], b_sl.shape[0],
-            c.data_ptr(), n, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+            ptr, c.stride(-2), _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
             torch.cuda.current_stream(a_sl.device).cuda_stream))
         return c
 
@@ -78,9 +82,38 @@ def _check_args(dtype, num_splits, slice_dtype):
         f"unsupported input dtype: {dtype}"
 
 
+def weighted_rows(m: int, world: int, root: int = 0, root_discount: int = 0,
+                  align: int = 128) -> list:
+    """Row counts per rank: balanced in blocks of ``align`` rows, with about
+    ``root_discount`` rows (times (world - 1) / world) moved off the root,
+    which also splits and broadcasts B."""
+    blocks = (m + align - 1) // align
+    if world == 1:
+        return [m]
+    root_blocks = max(0, round((m / world - root_discount * (world - 1) / world) / align))
+    root_blocks = min(root_blocks, blocks)
+    rest = blocks - root_blocks
+    counts = [0] * world
+    others = [r for r in range(world) if r != root]
+    for i, r in enumerate(others):
+        counts[r] = rest // len(others) + (1 if i < rest % len(others) else 0)
+    counts[root] = root_blocks
+    rows = [c * align for c in counts]
+    # the last rank that has rows absorbs the ragged end
+    excess = sum(rows) - m
+    for r in reversed(range(world)):
+        if excess <= 0:
+            break
+        take = min(excess, rows[r])
+        rows[r] -= take
+        excess -= take
+    return rows
+
+
 def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_splits: int = 3,
                        slice_dtype: torch.dtype = torch.float16, *, root: int = 0,
                        group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
+                       chunks: Optional[int] = None,
                        backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B, A sharded by rows, B on ``root`` only.
 
@@ -88,6 +121,10 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
     rank, including 0); the root passes B (K, N), the others may pass None.
     Returns this rank's rows of C (M_local, N) in the input dtype, equal bit
     for bit to the same rows of the single-GPU ``ozaki_matmul``.
+
+    B travels in ``chunks`` column blocks (multiples of 256 columns): the root
+    splits block c and starts its broadcast before splitting block c + 1, and
+    every rank starts the GEMM of block c as soon as it has arrived.
     """
     backend = backend or Backend()
     dev = A_local.device
@@ -104,23 +141,37 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
                                dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
     mode = _residual_mode(residual, num_splits, A_local.dtype)
     ld = _lib_row(k, slice_dtype)
-    if rank == root:
-        B3 = B.reshape(1, k, n)
-        b_sl, b_sc = backend.split(B3, B3.stride(2), B3.stride(1), n, k, num_splits, alpha,
-                                   slice_dtype, mode)
-    else:
-        b_sl = torch.empty((1, num_splits, n, ld), dtype=slice_dtype, device=dev)
-        b_sc = torch.empty((1, num_splits, n), dtype=torch.float32, device=dev)
-    # broadcast B's slices while this rank splits its rows of A
-    w1 = dist.broadcast(b_sl, src=root, group=group, async_op=True)
-    w2 = dist.broadcast(b_sc, src=root, group=group, async_op=True)
+    if chunks is None:
+        chunks = 1
+    blocks = (n + 255) // 256
+    chunks = max(1, min(chunks, blocks))
+    bounds = []
+    for c in range(chunks):
+        b0, b1 = block_range(blocks, chunks, c)
+        bounds.append((b0 * 256, min(n, b1 * 256)))
+    pieces, works = [], []
+    for c0, c1 in bounds:
+        nc = c1 - c0
+        if rank == root:
+            Bc = B[:, c0:c1].reshape(1, k, nc)
+            b_sl, b_sc = backend.split(Bc, Bc.stride(2), Bc.stride(1), nc, k, num_splits, alpha,
+                                       slice_dtype, mode)
+        else:
+            b_sl = torch.empty((1, num_splits, nc, ld), dtype=slice_dtype, device=dev)
+            b_sc = torch.empty((1, num_splits, nc), dtype=torch.float32, device=dev)
+        works.append((dist.broadcast(b_sl, src=root, group=group, async_op=True),
+                      dist.broadcast(b_sc, src=root, group=group, async_op=True)))
+        pieces.append((b_sl, b_sc))
+    # this rank's rows of A are split while the blocks of B travel
     A3 = A_local.reshape(1, m_loc, k)
     a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
                                slice_dtype, mode)
-    w1.wait()
-    w2.wait()
-    c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
-                     skip_tail)
+    c = torch.empty((1, m_loc, n), dtype=A_local.dtype, device=dev)
+    for (c0, c1), (b_sl, b_sc), (w1, w2) in zip(bounds, pieces, works):
+        w1.wait()
+        w2.wait()
+        backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, c1 - c0, k, num_splits, A_local.dtype,
+                     skip_tail, out=c, col0=c0)
     return c.reshape(m_loc, n)
 
 

@@ -41,14 +41,18 @@ class OracleBackend:
         return out, torch.from_numpy(sc)
 
     def gemm(self, a_sl, b_sl, a_sc, b_sc, batch, m, n, k, s, out_dtype, skip_tail,
-             a_idx=None, b_idx=None):
+             a_idx=None, b_idx=None, out=None, col0=0):
         ai = a_idx.long() if a_idx is not None else torch.arange(batch)
         bi = b_idx.long() if b_idx is not None else torch.arange(batch)
         a = a_sl[ai, ..., :k].numpy()
         b = b_sl[bi, ..., :k].numpy()
-        c = oracle.cross_gemm(a, b, a_sc[ai].numpy(), b_sc[bi].numpy(), KIND[a_sl.dtype],
-                              KIND[out_dtype], skip_tail)
-        return torch.from_numpy(np.ascontiguousarray(c))
+        c = torch.from_numpy(np.ascontiguousarray(oracle.cross_gemm(
+            a, b, a_sc[ai].numpy(), b_sc[bi].numpy(), KIND[a_sl.dtype], KIND[out_dtype],
+            skip_tail)))
+        if out is None:
+            return c
+        out[..., col0:col0 + n] = c
+        return out
 
 
 def free_port():
@@ -97,6 +101,11 @@ def case_mrows(rank, world, out_dir):
     c = ozd.ozaki_matmul_mrows(A[lo:hi], B if rank == 0 else None, 4, torch.int8,
                                backend=OracleBackend())
     np.save(os.path.join(out_dir, f"c{rank}.npy"), c.numpy())
+    # the same through three broadcast blocks of B's columns
+    B2 = law(g, (64, 600))
+    c2 = ozd.ozaki_matmul_mrows(A[lo:hi], B2 if rank == 0 else None, 4, torch.int8, chunks=3,
+                                backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"d{rank}.npy"), c2.numpy())
 
 
 def case_batches(rank, world, out_dir):
@@ -147,6 +156,9 @@ def test_mrows_two_ranks_bit_identical(tmp_path):
     B = law(g, (64, 23))
     want = oracle.ozaki_matmul(A.numpy(), B.numpy(), 4, "int8", "fp64")
     assert np.array_equal(c, want)
+    B2 = law(g, (64, 600))
+    d = np.concatenate([np.load(tmp_path / f"d{r}.npy") for r in range(2)])
+    assert np.array_equal(d, oracle.ozaki_matmul(A.numpy(), B2.numpy(), 4, "int8", "fp64"))
 
 
 def test_batches_two_ranks_cover_the_broadcast(tmp_path):
@@ -171,3 +183,12 @@ def test_root_failure_is_reported_not_hung(tmp_path):
     msg = (tmp_path / "peer_error.txt").read_text()
     assert msg != "NO ERROR", msg              # the peer saw an error ...
     assert time.time() - t0 < 110              # ... within the timeout, no hang
+
+
+def test_weighted_rows_partition():
+    for m in [1, 37, 128, 1000, 8192, 16384]:
+        for world in [1, 2, 3, 8]:
+            for disc in [0, 100, 768, 10 ** 6]:
+                rows = ozd.weighted_rows(m, world, 0, disc)
+                assert sum(rows) == m and min(rows) >= 0 and len(rows) == world
+    assert ozd.weighted_rows(8192, 8, 0, 768)[0] < 8192 // 8

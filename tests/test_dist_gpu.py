@@ -41,6 +41,9 @@ def _worker(rank, world, port, out_dir):
                                    torch.int8)
         want = oz.ozaki_matmul(A.to(dev), B.to(dev), 4, torch.int8)[lo:hi]
         ok1 = torch.equal(c, want)
+        c3 = ozd.ozaki_matmul_mrows(A[lo:hi].to(dev), B.to(dev) if rank == 0 else None, 4,
+                                    torch.int8, chunks=2)
+        ok1 = ok1 and torch.equal(c3, want)
         A4 = torch.randn(4, 1, 64, 96, generator=g, dtype=torch.float64)
         B4 = torch.randn(1, 3, 96, 40, generator=g, dtype=torch.float64)
         cb, s0, s1 = ozd.ozaki_matmul_batches(A4.to(dev), B4.to(dev), 3, torch.float16)
