@@ -206,6 +206,9 @@ def main():
                     help="multi-GPU: rows of A moved off rank 0, which also splits B")
     ap.add_argument("--chunks", type=int, default=0,
                     help="multi-GPU: column blocks B is broadcast in (0 = by GPU count)")
+    ap.add_argument("--config", default="C3", choices=sorted(CONFIGS),
+                    help="benchmark configuration (C3 = the headline)")
+    ap.add_argument("--num-splits", type=int, default=0, help="override the config's s")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, DGEMM or CPU legs): the ncu command line")
     args = ap.parse_args()
@@ -222,48 +225,107 @@ def main():
     run_single(args)
 
 
+# the benchmark configurations of BASELINE.json (C3 is the headline)
+CONFIGS = {
+    "C1": dict(a=(256, 256), b=(256, 256), dtype=torch.float32, slice=torch.float16, s=2,
+               law="uniform", seed=0,
+               desc="FP32->FP16 Ozaki s=2, 256^3, U(-1,1) seed 0"),
+    "C2": dict(a=(8192, 8192), b=(8192, 8192), dtype=torch.float32, slice=torch.float16, s=2,
+               law="normal", seed=1, desc="FP32->FP16 Ozaki s=2, 8192^3, N(0,1) seed 1"),
+    "C3": dict(a=(8192, 8192), b=(8192, 8192), dtype=torch.float64, slice=torch.int8, s=4,
+               law=1.0, seed=2, desc=WORKLOAD),
+    "C4": dict(a=(16, 1, 2048, 4096), b=(1, 8, 4096, 2048), dtype=torch.float64,
+               slice=torch.float16, s=3, law="normal", seed=3,
+               desc="FP64->FP16 Ozaki s=3, (16,1,2048,4096)x(1,8,4096,2048) -> 128 GEMMs, "
+                    "N(0,1) seed 3"),
+    "C5": dict(a=(16384, 16384), b=(16384, 16384), dtype=torch.float64, slice=torch.int8, s=4,
+               law=4.0, seed=4,
+               desc="FP64->INT8 Ozaki s=4, 16384^3, x=(U(0,1)-0.5)*exp(4 N(0,1)) seed 4"),
+}
+SLICE_NAME = {torch.int8: "int8", torch.float16: "fp16", torch.bfloat16: "bf16",
+              torch.float32: "fp32"}
+DTYPE_NAME = {torch.float64: "fp64", torch.float32: "fp32", torch.float16: "fp16",
+              torch.bfloat16: "bf16"}
+
+
+def config_inputs(cfg):
+    """Host operands of a configuration from its seeded CPU generator."""
+    g = torch.Generator().manual_seed(cfg["seed"])
+    law = cfg["law"]
+    if law == "uniform":
+        a = torch.rand(cfg["a"], generator=g, dtype=torch.float64) * 2 - 1
+        b = torch.rand(cfg["b"], generator=g, dtype=torch.float64) * 2 - 1
+    elif law == "normal":
+        a = torch.randn(cfg["a"], generator=g, dtype=torch.float64)
+        b = torch.randn(cfg["b"], generator=g, dtype=torch.float64)
+    else:   # (U(0,1) - 0.5) * exp(sigma N(0,1)); draw order A's U, A's N, B's U, B's N
+        ua = torch.rand(cfg["a"], generator=g, dtype=torch.float64)
+        na = torch.randn(cfg["a"], generator=g, dtype=torch.float64)
+        ub = torch.rand(cfg["b"], generator=g, dtype=torch.float64)
+        nb = torch.randn(cfg["b"], generator=g, dtype=torch.float64)
+        a, b = (ua - 0.5) * torch.exp(law * na), (ub - 0.5) * torch.exp(law * nb)
+    return a.to(cfg["dtype"]), b.to(cfg["dtype"])
+
+
 def run_single(args):
+    import math
+
     import ozaki_triton_b200 as oz
     from ozaki_triton_b200 import _lib
+    from ozaki_triton_b200.api import _OZ_DTYPE, _batch_index, _split_lines
 
+    name = args.config
+    cfg = CONFIGS[name]
+    s = args.num_splits or cfg["s"]
+    sd, dt = cfg["slice"], cfg["dtype"]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    a_h, b_h = make_inputs()
+    a_h, b_h = config_inputs(cfg)
     a = a_h.to(dev)
     b = b_h.to(dev)
     stream = torch.cuda.current_stream()
-
-    # per-step device timing of the dominant kernel: events around the GEMM
+    Mm, Kk = a.shape[-2:]
+    Nn = b.shape[-1]
+    a_batch, b_batch = tuple(a.shape[:-2]), tuple(b.shape[:-2])
+    full = tuple(torch.broadcast_shapes(a_batch, b_batch))
+    BN = math.prod(full)
+    BA, BB = math.prod(a_batch), math.prod(b_batch)
+    a_idx = _batch_index(a_batch, full, dev)
+    b_idx = _batch_index(b_batch, full, dev)
+    A3 = a.reshape(BA, Mm, Kk)
+    B3 = b.reshape(BB, Kk, Nn)
+    residual = _lib.OZ_RESIDUAL_COMPAT if s <= 4 else _lib.OZ_RESIDUAL_EXACT
+    alpha = oz.compute_split_bits(Kk, sd, oz.select_dot_accum_dtype(sd))
     gemm_events = []
 
     def step(record: bool):
-        alpha = oz.compute_split_bits(K, torch.int8, torch.int32)
-        from ozaki_triton_b200.api import _split_lines, _OZ_DTYPE
-        b_sl, b_sc = _split_lines(b.reshape(1, K, N), 1, N, N, K, NUM_SPLITS, alpha,
-                                  torch.int8, _lib.OZ_RESIDUAL_COMPAT)
-        a_sl, a_sc = _split_lines(a.reshape(1, M, K), K, 1, M, K, NUM_SPLITS, alpha,
-                                  torch.int8, _lib.OZ_RESIDUAL_COMPAT)
-        c = torch.empty((M, N), dtype=torch.float64, device=dev)
+        """One ozaki_matmul, with the cross-GEMM timed by events."""
+        b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), Nn, Kk, s, alpha, sd, residual)
+        a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), Mm, Kk, s, alpha, sd, residual)
+        c = torch.empty((BN, Mm, Nn), dtype=dt, device=dev)
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
         _lib.check(_lib.load().oz_cross_gemm(
-            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), 1, M, N, K,
-            a_sl.shape[-1], NUM_SPLITS, _OZ_DTYPE[torch.int8], _OZ_DTYPE[torch.float64],
-            None, None, 1, 1, c.data_ptr(), N, 0, stream.cuda_stream))
+            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), BN, Mm, Nn, Kk,
+            a_sl.shape[-1], s, _OZ_DTYPE[sd], _OZ_DTYPE[dt],
+            a_idx.data_ptr() if a_idx is not None else None,
+            b_idx.data_ptr() if b_idx is not None else None, BA, BB, c.data_ptr(), Nn, 0,
+            stream.cuda_stream))
         if record:
             e1.record(stream)
             gemm_events.append((e0, e1))
         return c
 
-    # the public call, checked once against the step above
     for _ in range(args.warmup):
         step(False)
-    c_api = oz.ozaki_matmul(a, b, num_splits=NUM_SPLITS, slice_dtype=torch.int8)
+    # the timed step is the public call's work: check it once against the public call
+    c_api = oz.ozaki_matmul(a, b, num_splits=s, slice_dtype=sd)
     c_step = step(False)
     torch.cuda.synchronize()
-    assert torch.equal(c_api, c_step)
+    assert torch.equal(c_api.reshape(c_step.shape), c_step)
+    del c_api
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -276,42 +338,46 @@ def run_single(args):
         torch.cuda.synchronize()
     ms = start.elapsed_time(end) / args.steps
     gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
-    flops = 2.0 * M * N * K
+    flops = 2.0 * BN * Mm * Nn * Kk
     value = flops / (ms * 1e-3) / 1e12
-    pairs = NUM_SPLITS * NUM_SPLITS
+    pairs = s * s
     bf16_peak, hbm_peak, peak_src = peaks()
-    int8_peak = 2.0 * bf16_peak
+    tensor_peak = 2.0 * bf16_peak if sd == torch.int8 else (bf16_peak if sd != torch.float32
+                                                            else bf16_peak / 2.0)
+    peak_note = {torch.int8: "2x", torch.float16: "1x", torch.bfloat16: "1x",
+                 torch.float32: "0.5x"}[sd]
     achieved = pairs * flops / (gemm_ms * 1e-3) / 1e12
 
-    # accuracy and speed next to cuBLAS DGEMM
-    rel_err = dgemm_tflops = None
+    # accuracy against an fp64 matmul, and the native GEMM of the input dtype
+    rel_err = native_tflops = None
     if not args.no_dgemm:
-        ref = a @ b
-        c = step(False)
+        ref = torch.matmul(a.double(), b.double())
+        c = step(False).reshape(ref.shape).double()
         rel_err = ((c - ref).norm() / ref.norm()).item()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
+        del ref, c
+        torch.backends.cuda.matmul.allow_tf32 = False
         for _ in range(2):
             torch.matmul(a, b)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(3):
             torch.matmul(a, b)
         t1.record(stream)
         torch.cuda.synchronize()
-        dgemm_tflops = flops / (t0.elapsed_time(t1) / 3 * 1e-3) / 1e12
-        del ref, c
+        native_tflops = flops / (t0.elapsed_time(t1) / 3 * 1e-3) / 1e12
 
     # end to end through the public call with host operands
     e2e = None
     if not args.no_e2e:
         a_pin = a_h.pin_memory()
         b_pin = b_h.pin_memory()
-        c_pin = torch.empty((M, N), dtype=torch.float64).pin_memory()
+        c_pin = torch.empty((*full, Mm, Nn), dtype=dt).pin_memory()
 
         def e2e_step():
             ad = a_pin.to(dev, non_blocking=True)
             bd = b_pin.to(dev, non_blocking=True)
-            cd = oz.ozaki_matmul(ad, bd, num_splits=NUM_SPLITS, slice_dtype=torch.int8)
+            cd = oz.ozaki_matmul(ad, bd, num_splits=s, slice_dtype=sd)
             c_pin.copy_(cd, non_blocking=True)
 
         for _ in range(2):
@@ -327,32 +393,40 @@ def run_single(args):
         torch.cuda.synchronize()
         e2e_ms = s0.elapsed_time(s1) / e2e_steps
         e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
-               "ms_per_step": e2e_ms, "h2d_bytes_per_step": 2 * M * K * 8,
-               "d2h_bytes_per_step": M * N * 8}
+               "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": a_h.numel() * a_h.element_size() +
+               b_h.numel() * b_h.element_size(),
+               "d2h_bytes_per_step": c_pin.numel() * c_pin.element_size()}
 
-    traffic = committed_traffic()
+    traffic = committed_traffic() if name == "C3" and s == 4 else None
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps,
+        "metric": METRIC if name == "C3" else f"emulated TFLOPS (2MNK/t), {cfg['desc']}",
+        "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "num_splits": NUM_SPLITS,
-                   "slice_dtype": "int8", "input_dtype": "fp64", "residual": "compat",
-                   "l2": "no flush: A and B are 512 MiB each, larger than the 126 MB L2",
+        "vs_baseline": None, "dtype": SLICE_NAME[sd], "data": "synthetic",
+        "config": {"workload": cfg["desc"], "name": name, "A": list(a.shape), "B": list(b.shape),
+                   "num_splits": s, "slice_dtype": SLICE_NAME[sd],
+                   "input_dtype": DTYPE_NAME[dt],
+                   "residual": "compat" if residual == _lib.OZ_RESIDUAL_COMPAT else "exact",
+                   "l2": "no flush: operands larger than the 126 MB L2" if a.numel() * a.element_size() > 126e6
+                   else "operands smaller than L2 (small config)",
                    "parallelism": "1 GPU"},
-        "roofline": {"bound": "tensor", "kernel": "cross_gemm_kernel<i8,f64,128>",
-                     "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                     "frac": achieved / int8_peak,
-                     "peak_source": f"2x {peak_src} dense bf16 ({bf16_peak} TF/s, "
-                                    "MEASURED_PEAKS.json); B200 dense int8 = 2x bf16",
+        "roofline": {"bound": "tensor", "kernel": f"cross_gemm_kernel<{SLICE_NAME[sd]}>",
+                     "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tensor_peak,
+                     "peak_source": f"{peak_note} {peak_src} dense bf16 ({bf16_peak} TF/s, "
+                                    "MEASURED_PEAKS.json); B200 dense int8 = 2x bf16, "
+                                    "tf32 = 0.5x",
                      "gemm_ms": gemm_ms,
                      "traffic": traffic.get("cross_gemm_bytes_per_launch") if traffic else None},
-        "rel_err_vs_dgemm": rel_err,
-        "cublas_dgemm_tflops": dgemm_tflops,
+        "rel_err_vs_fp64": rel_err,
+        "native_gemm_tflops": native_tflops,
+        "native_gemm": "cuBLAS DGEMM" if dt == torch.float64 else "cuBLAS SGEMM (no TF32)",
         "clocks": clk.summary(),
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": (3 + (1 if BB * Nn * Kk > 0 else 0)) * args.steps,
         "e2e": e2e,
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and name == "C3":
         line["cpu_baseline"] = cpu_baseline_sample()
     print(json.dumps(line), flush=True)
 
