@@ -175,12 +175,14 @@ struct LevelP {
   float scale;      // stored scale 2^e
   double inv_d;     // 2^-e
   float inv1, inv2; // 2^-e == inv1 * inv2, both exact floats
+  bool big;         // 2^-e is not a float: two multiplies
   __device__ __forceinline__ void init(float row_max, int alpha) {
     const float m = fmaxf(1e-38f, row_max);
     const int e = ceil_log2_table(m) - alpha;     // e in [-149, 127]
     scale = pow2f(e);
     inv_d = pow2d(-e);
-    if (-e > 127) {
+    big = -e > 127;
+    if (big) {
       inv1 = 18446744073709551616.0f;             // 2^64
       inv2 = pow2f(-e - 64);
     } else {
@@ -253,35 +255,38 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f64(double r, const Le
   return q;
 }
 
-// Integer rounding of a = min(|x|, 130) as a float holding
-// floor(a + 0.5) + 1.5 * 2^23, clamped to 127 (x >= 0) / 128 (x < 0).
-// fl32(a + 0.5) has the floor of the exact sum for every fp32 a except
-// 0.5 - 2^-25 (checked exhaustively over all fp32 values below 512): that
-// one input is folded to 0 when EXACT_HALF (fp64 reference arithmetic) and
-// kept (fp32 reference arithmetic rounds it up) otherwise.  Pre-clamping |x|
-// to 130 changes no result (the reference saturates beyond 128) and keeps
-// the magic-number rounding exact for any alpha.
-template <bool EXACT_HALF>
-__device__ __forceinline__ float round_half_away_magic(float a, bool neg) {
-  const float t = __fadd_rn(a, 0.5f);
-  float y = __fadd_rn(t, kMagicF);                        // nearest integer of t, + M
-  y = (__fsub_rn(y, kMagicF) > t) ? __fsub_rn(y, 1.0f) : y;   // -> floor(t) + M
-  if (EXACT_HALF) y = (a == __int_as_float(0x3EFFFFFF)) ? kMagicF : y;
-  return fminf(y, neg ? kMagicF + 128.0f : kMagicF + 127.0f);
+// Round half away from zero of an fp32 x with |x| < 2^22, clamped to
+// [-128, 127], as the float y = q + 1.5 * 2^23 (exact).  x + M rounds x to
+// the nearest integer with ties to even; d = x - RN(x) is exact, and a tie
+// rounded toward zero (|d| == 0.5 with |RN(x)| < |x|) is moved away by 2d.
+// The int8 value is the low byte of y's bit pattern (M's low byte is 0).
+__device__ __forceinline__ float rna_magic(float x) {
+  float y = __fadd_rn(x, kMagicF);
+  const float q = __fsub_rn(y, kMagicF);
+  const float d = __fsub_rn(x, q);
+  if (fabsf(d) == 0.5f && fabsf(q) < fabsf(x)) y = __fmaf_rn(2.0f, d, y);
+  return fmaxf(fminf(y, kMagicF + 127.0f), kMagicF - 128.0f);
 }
 
-// level >= 1 of an fp64 input (fp32-valued residual, fp64 reference arithmetic)
-template <int SK>
+// x = r * 2^-e in fp32: one multiply, or two when 2^-e exceeds the float range
+template <bool BIG>
+__device__ __forceinline__ float scale_down(float r, const LevelP &lv) {
+  if constexpr (BIG) return __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);
+  else return __fmul_rn(r, lv.inv2);
+}
+
+// level >= 1 of an fp64 input (fp32-valued residual, fp64 reference
+// arithmetic): x is exact and the reference's fp64 "x + 0.5, truncate" is
+// exact rounding half away from zero (x + 0.5 needs at most 33 bits whenever
+// the result can be nonzero)
+template <int SK, bool BIG>
 __device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, const LevelP &lv,
                                                                     bool upd) {
-  const float x = __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);   // exact
+  const float x = scale_down<BIG>(r, lv);
   if constexpr (SK == OZ_I8) {
-    const bool neg = x < 0.f;
-    const float y = round_half_away_magic<true>(fminf(fabsf(x), 130.f), neg);
-    const float qa = __fsub_rn(y, kMagicF);                    // |q| as float
-    const int na = __float_as_int(y) - kMagicFBits;            // |q|
-    if (upd) r = __fmaf_rn(-copysignf(qa, x), lv.scale, r);
-    return (int8_t)(neg ? -na : na);
+    const float y = rna_magic(x);
+    if (upd) r = __fmaf_rn(-__fsub_rn(y, kMagicF), lv.scale, r);   // exact
+    return (int8_t)(__float_as_uint(y) & 0xFFu);
   } else {
     const auto q = slice_from_f32<SK>(x);
     if (upd) r = __fmaf_rn(-slice_to_f32<SK>(q), lv.scale, r);
@@ -289,19 +294,19 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, co
   }
 }
 
-// every level of a non-fp64 input (fp32 residual, fp32 reference arithmetic)
-template <int SK>
+// every level of a non-fp64 input (fp32 residual, fp32 reference arithmetic):
+// trunc(fl32(x +- 0.5)) = sign(x) * floor(fl32(|x| + 0.5)), which is rounding
+// half away from zero except for |x| = 0.5 - 2^-25, where fl32(|x| + 0.5)
+// rounds up to 1 (checked exhaustively over every fp32 value below 512)
+template <int SK, bool BIG>
 __device__ __forceinline__ typename SliceT<SK>::type step_f32_rd(float &r, const LevelP &lv,
                                                                  bool upd) {
-  const float x = __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);   // == r / scale, rounded once
+  const float x = scale_down<BIG>(r, lv);   // == r / scale, rounded once
   if constexpr (SK == OZ_I8) {
-    // trunc(fl32(x +- 0.5)) == sign(x) * floor(fl32(|x| + 0.5))
-    const bool neg = x < 0.f;
-    const float y = round_half_away_magic<false>(fminf(fabsf(x), 130.f), neg);
-    const float qa = __fsub_rn(y, kMagicF);
-    const int na = __float_as_int(y) - kMagicFBits;
-    if (upd) r = __fsub_rn(r, __fmul_rn(copysignf(qa, x), lv.scale));
-    return (int8_t)(neg ? -na : na);
+    float y = rna_magic(x);
+    if (fabsf(x) == __int_as_float(0x3EFFFFFF)) y = kMagicF + copysignf(1.0f, x);
+    if (upd) r = __fsub_rn(r, __fmul_rn(__fsub_rn(y, kMagicF), lv.scale));
+    return (int8_t)(__float_as_uint(y) & 0xFFu);
   } else {
     const auto q = slice_from_f32<SK>(x);
     if (upd) r = __fsub_rn(r, __fmul_rn(slice_to_f32<SK>(q), lv.scale));
@@ -338,8 +343,12 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
     else vf[i] = InTraits<TIn>::to_float(v);
   }
 
-  template <typename Reduce, typename Emit, typename Scale>
-  __device__ __forceinline__ void run(int s, int alpha, Reduce reduce, Emit emit, Scale put_scale) {
+  // emit(l, i, q) stores one slice element and must not synchronise (it runs
+  // inside data-dependent branches); end_level(l) runs once per level on
+  // every thread, after all of that level's emits.
+  template <typename Reduce, typename Emit, typename Scale, typename EndLevel>
+  __device__ __forceinline__ void run(int s, int alpha, Reduce reduce, Emit emit, Scale put_scale,
+                                      EndLevel end_level) {
     for (int l = 0; l < s; ++l) {
       const bool upd = l < s - 1;
       const bool on_f64 = F64IN && (EXACT || l == 0);
@@ -370,15 +379,24 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
             emit(l, i, q);
           }
         }
+      } else if (!lv.big) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          ST q;
+          if constexpr (F64IN) q = step_f32_exact<SK, false>(vf[i], lv, upd);
+          else q = step_f32_rd<SK, false>(vf[i], lv, upd);
+          emit(l, i, q);
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           ST q;
-          if constexpr (F64IN) q = step_f32_exact<SK>(vf[i], lv, upd);
-          else q = step_f32_rd<SK>(vf[i], lv, upd);
+          if constexpr (F64IN) q = step_f32_exact<SK, true>(vf[i], lv, upd);
+          else q = step_f32_rd<SK, true>(vf[i], lv, upd);
           emit(l, i, q);
         }
       }
+      end_level(l);
     }
   }
 };
@@ -505,7 +523,7 @@ __global__ void __launch_bounds__(kRowCTA, 1)
         if ((wmask >> c) & 1) *reinterpret_cast<Pack<ST, VEC> *>(dl + c * T * VEC) = pq;
       }
     };
-    ll.run(s, alpha, reduce, emit, put_scale);
+    ll.run(s, alpha, reduce, emit, put_scale, [](int) {});
   }
 }
 
@@ -626,27 +644,26 @@ __global__ void __launch_bounds__(kColCTA, 1)
     Pack<ST, 4> pq;
     auto emit = [&](int l, int i, ST q) {
       pq.e[i & 3] = q;
-      if ((i & 3) == 3) {
+      if ((i & 3) == 3)
         *reinterpret_cast<Pack<ST, 4> *>(outst + c * PITCH + 4 * (g + G * (i >> 2)) * sizeof(ST)) =
             pq;
-        if (i == V - 1) {
-          // level complete in shared memory: coalesced 16-byte stores
-          __syncthreads();
-          constexpr int CPL = KC * (int)sizeof(ST) / 16;
-          ST *dst = out + ((int64_t)b * s + l) * lines * (int64_t)ld;
-          for (int id = threadIdx.x; id < W * CPL; id += kColCTA) {
-            const int cc = id / CPL, off = id % CPL;
-            const int nn = pn * W + cc;
-            const int k0 = kbase + off * 16 / (int)sizeof(ST);
-            if (nn < lines && k0 < ld)
-              *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(dst + (int64_t)nn * ld + k0)) =
-                  *reinterpret_cast<const uint4 *>(outst + cc * PITCH + off * 16);
-          }
-          __syncthreads();
-        }
-      }
     };
-    ll.run(s, alpha, reduce, emit, put_scale);
+    auto end_level = [&](int l) {
+      // level complete in shared memory: coalesced 16-byte stores
+      __syncthreads();
+      constexpr int CPL = KC * (int)sizeof(ST) / 16;
+      ST *dst = out + ((int64_t)b * s + l) * lines * (int64_t)ld;
+      for (int id = threadIdx.x; id < W * CPL; id += kColCTA) {
+        const int cc = id / CPL, off = id % CPL;
+        const int nn = pn * W + cc;
+        const int k0 = kbase + off * 16 / (int)sizeof(ST);
+        if (nn < lines && k0 < ld)
+          *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(dst + (int64_t)nn * ld + k0)) =
+              *reinterpret_cast<const uint4 *>(outst + cc * PITCH + off * 16);
+      }
+      __syncthreads();
+    };
+    ll.run(s, alpha, reduce, emit, put_scale, end_level);
   }
   if (CL > 1) cluster_sync();   // no CTA leaves while peers may still address it
 }
@@ -979,6 +996,9 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
   if (slice_dtype != OZ_I8 && slice_dtype != OZ_F16 && slice_dtype != OZ_BF16 &&
       slice_dtype != OZ_F32)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported slice dtype %d", slice_dtype);
+  // int8 slices saturate at 2^7 anyway; the rounding needs |x| < 2^22
+  if (slice_dtype == OZ_I8 && alpha > 21)
+    return set_error(OZ_ERR_INVALID, "alpha %d too large for int8 slices (at most 21)", alpha);
   if (in_dtype != OZ_F64 && in_dtype != OZ_F32 && in_dtype != OZ_F16 && in_dtype != OZ_BF16)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported input dtype %d", in_dtype);
   if (residual_mode != OZ_RESIDUAL_COMPAT && residual_mode != OZ_RESIDUAL_EXACT)
