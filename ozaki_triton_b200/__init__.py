@@ -14,6 +14,7 @@ from .api import (  # noqa: F401
     cross_gemm,
     device_status,
     ozaki_matmul,
+    ozaki_matmul_from_host,
     select_dot_accum_dtype,
     select_out_accum_dtype,
     slice_row_elems,
@@ -22,7 +23,7 @@ from .api import (  # noqa: F401
 from ._lib import OzakiError, OzakiLibraryError, load as load_library, version  # noqa: F401
 
 __all__ = [
-    "ozaki_matmul", "split_matrix", "cross_gemm", "compute_split_bits",
+    "ozaki_matmul", "ozaki_matmul_from_host", "split_matrix", "cross_gemm", "compute_split_bits",
     "select_dot_accum_dtype", "select_out_accum_dtype", "slice_row_elems",
     "device_status", "OzakiError", "OzakiLibraryError", "load_library", "version",
 ]

@@ -298,6 +298,116 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     return C.view(out_shape)
 
 
+_STREAMS = {}
+
+
+def _side_streams(dev: torch.device):
+    """Three side streams per device, created once (copy-in, compute, copy-out)."""
+    key = dev.index
+    if key not in _STREAMS:
+        _STREAMS[key] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return _STREAMS[key]
+
+
+def ozaki_matmul_from_host(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
+                           slice_dtype: torch.dtype = torch.float16, *,
+                           device: Optional[torch.device] = None, row_blocks: int = 16,
+                           skip_tail: bool = False, residual: Optional[str] = "auto",
+                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``ozaki_matmul`` for operands in (pinned) host memory; returns C on the host.
+
+    The host<->device copies are pipelined with the device work: B is copied
+    first and split as soon as it has arrived, A follows in ``row_blocks`` row
+    blocks whose splits and GEMMs start as each block lands, and every block of
+    C goes back while the next is computed (the link is full duplex).  All
+    work is enqueued on side streams joined to the current stream: like a
+    ``non_blocking`` copy, the returned tensor is ready once the current CUDA
+    stream has been synchronised.  Operands that are not 2-D, not contiguous or
+    not pinned take the plain path (copy, ``ozaki_matmul``, copy back).
+    """
+    assert A.dtype == B.dtype, f"A/B dtype mismatch: {A.dtype} vs {B.dtype}"
+    assert A.dtype in INPUT_DTYPES, f"unsupported input dtype: {A.dtype}"
+    assert slice_dtype in SLICE_DTYPE_INFO, f"unsupported slice dtype: {slice_dtype}"
+    assert 1 <= num_splits <= MAX_SPLITS, \
+        f"num_splits must be in [1, {MAX_SPLITS}], got {num_splits}"
+    dev = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    main = torch.cuda.current_stream(dev)
+    if (A.dim() != 2 or B.dim() != 2 or not A.is_contiguous() or not B.is_contiguous()
+            or not A.is_pinned() or not B.is_pinned()):
+        c = ozaki_matmul(A.to(dev, non_blocking=True), B.to(dev, non_blocking=True), num_splits,
+                         slice_dtype, skip_tail=skip_tail, residual=residual)
+        host = out if out is not None else torch.empty(c.shape, dtype=c.dtype, pin_memory=True)
+        host.copy_(c, non_blocking=True)
+        return host
+    M, K = A.shape
+    K2, N = B.shape
+    assert K == K2, f"contraction dim mismatch: A K={K}, B K={K2}"
+    dt = A.dtype
+    C_host = out if out is not None else torch.empty((M, N), dtype=dt, pin_memory=True)
+    if M == 0 or N == 0:
+        return C_host
+    alpha = compute_split_bits(K, slice_dtype=slice_dtype,
+                               dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
+    mode = _residual_mode(residual, num_splits, dt)
+    h2d, comp, d2h = _side_streams(dev)
+    for st in (h2d, comp, d2h):
+        st.wait_stream(main)
+    lib = _lib.load()
+    blocks = max(1, min(row_blocks, (M + 127) // 128))
+    bounds = []
+    for i in range(blocks):
+        r0 = (M * i // blocks) // 128 * 128 if i else 0
+        r1 = M if i == blocks - 1 else (M * (i + 1) // blocks) // 128 * 128
+        if r1 > r0:
+            bounds.append((r0, r1))
+    with torch.cuda.stream(h2d):
+        Bd = B.to(dev, non_blocking=True)
+        ev_b = torch.cuda.Event()
+        ev_b.record(h2d)
+        Ad = torch.empty((M, K), dtype=dt, device=dev)
+        ev_a = []
+        for r0, r1 in bounds:
+            Ad[r0:r1].copy_(A[r0:r1], non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(h2d)
+            ev_a.append(e)
+    Cd = torch.empty((M, N), dtype=dt, device=dev)
+    with torch.cuda.stream(comp):
+        comp.wait_event(ev_b)
+        B3 = Bd.reshape(1, K, N)
+        b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), N, K, num_splits, alpha,
+                                  slice_dtype, mode)
+        ev_c = []
+        for (r0, r1), e in zip(bounds, ev_a):
+            comp.wait_event(e)
+            A3 = Ad[r0:r1].reshape(1, r1 - r0, K)
+            a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), r1 - r0, K, num_splits,
+                                      alpha, slice_dtype, mode)
+            _lib.check(lib.oz_cross_gemm(
+                a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), 1, r1 - r0,
+                N, K, b_sl.shape[-1], num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[dt], None,
+                None, 1, 1, Cd[r0:r1].data_ptr(), N, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+                comp.cuda_stream))
+            ec = torch.cuda.Event()
+            ec.record(comp)
+            ev_c.append(ec)
+    with torch.cuda.stream(d2h):
+        for (r0, r1), e in zip(bounds, ev_c):
+            d2h.wait_event(e)
+            C_host[r0:r1].copy_(Cd[r0:r1], non_blocking=True)
+    # the caller's stream sees everything; memory used on streams other than
+    # the one it was allocated on is not reused before that work is done
+    main.wait_stream(d2h)
+    main.wait_stream(comp)
+    main.wait_stream(h2d)
+    Bd.record_stream(comp)
+    Ad.record_stream(comp)
+    Cd.record_stream(comp)
+    Cd.record_stream(d2h)
+    return C_host
+
+
 def device_status() -> int:
     """Synchronise the current stream and return (and clear) the kernels'
     timeout code (0 = none).  Raises OzakiError if a bound was hit."""

@@ -355,3 +355,24 @@ def test_split_columns_c_abi_workspace_and_cluster(use_ws, ik, sk, K):
     assert same_bits(got, rsl if sk == "int8" else rsl.astype(np.float32))
     # padding beyond K is zero
     assert not host(sl[..., K:]).any()
+
+
+@pytest.mark.parametrize("ik,sk,s,shape", [("fp64", "int8", 4, (1000, 900, 700)),
+                                           ("fp32", "fp16", 2, (520, 256, 384)),
+                                           ("fp64", "int8", 3, (100, 50, 64))])
+def test_from_host_pipeline_matches_device_call(ik, sk, s, shape):
+    """The pipelined host-operand call gives the device call's bits."""
+    M, N, K = shape
+    g = torch.Generator().manual_seed(M + N)
+    a = (torch.rand(M, K, generator=g, dtype=torch.float64) - 0.5).to(TDT[ik])
+    b = (torch.rand(K, N, generator=g, dtype=torch.float64) - 0.5).to(TDT[ik])
+    want = oz.ozaki_matmul(a.to(DEV), b.to(DEV), num_splits=s, slice_dtype=TDT[sk]).cpu()
+    for _ in range(2):
+        got = oz.ozaki_matmul_from_host(a.pin_memory(), b.pin_memory(), num_splits=s,
+                                        slice_dtype=TDT[sk], row_blocks=3)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    # unpinned / batched operands take the plain path
+    got = oz.ozaki_matmul_from_host(a, b, num_splits=s, slice_dtype=TDT[sk])
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
