@@ -376,3 +376,30 @@ def test_from_host_pipeline_matches_device_call(ik, sk, s, shape):
     got = oz.ozaki_matmul_from_host(a, b, num_splits=s, slice_dtype=TDT[sk])
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+
+
+def test_cuda_graph_capture_and_replay():
+    """ozaki_matmul enqueues only stream-ordered work (no host sync, no
+    allocation outside torch's allocator), so a step can be captured once
+    and replayed -- the launch-bound small shapes gain the most."""
+    g = torch.Generator().manual_seed(9)
+    a = torch.rand(256, 256, generator=g).to(DEV) * 2 - 1
+    b = torch.rand(256, 256, generator=g).to(DEV) * 2 - 1
+    want = oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.float16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):                       # warm up outside the capture
+            oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.float16)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.float16)
+    for scale in (1.0, 3.0):
+        a.mul_(scale)
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.float16)
+        assert torch.equal(out, ref)
+    assert oz.device_status() == 0
+    del graph
