@@ -255,17 +255,24 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f64(double r, const Le
   return q;
 }
 
-// Round half away from zero of an fp32 x with |x| < 2^22, clamped to
-// [-128, 127], as the float y = q + 1.5 * 2^23 (exact).  x + M rounds x to
-// the nearest integer with ties to even; d = x - RN(x) is exact, and a tie
-// rounded toward zero (|d| == 0.5 with |RN(x)| < |x|) is moved away by 2d.
-// The int8 value is the low byte of y's bit pattern (M's low byte is 0).
-__device__ __forceinline__ float rna_magic(float x) {
-  float y = __fadd_rn(x, kMagicF);
-  const float q = __fsub_rn(y, kMagicF);
-  const float d = __fsub_rn(x, q);
-  if (fabsf(d) == 0.5f && fabsf(q) < fabsf(x)) y = __fmaf_rn(2.0f, d, y);
-  return fmaxf(fminf(y, kMagicF + 127.0f), kMagicF - 128.0f);
+// Integer rounding of an fp32 x (|x| < 2^22) to q in [-128, 127], returned
+// as a float.  floor(t) for t >= 0 is the magic add rounded toward zero:
+// fl_rz(t + 1.5 * 2^23) = 1.5 * 2^23 + floor(t).
+//   EXACT_HALF (fp64 reference arithmetic, exact "|x| + 0.5"): t =
+//     fl_rz(|x| + 0.5) never rounds up across an integer, so floor(t) =
+//     floor(|x| + 0.5) exactly.
+//   otherwise (fp32 reference arithmetic): t = fl_rn(|x| + 0.5), exactly the
+//     reference's rounded sum, then truncated.
+template <bool EXACT_HALF>
+__device__ __forceinline__ float round_q(float x) {
+  const float a = fabsf(x);
+  const float t = EXACT_HALF ? __fadd_rz(a, 0.5f) : __fadd_rn(a, 0.5f);
+  const float qa = __fsub_rn(__fadd_rz(t, kMagicF), kMagicF);   // floor(t), exact
+  return fmaxf(fminf(copysignf(qa, x), 127.0f), -128.0f);
+}
+// the int8 bit pattern of an integer-valued float q in [-128, 127]
+__device__ __forceinline__ int8_t q_byte(float q) {
+  return (int8_t)(__float_as_uint(__fadd_rn(q, kMagicF)) & 0xFFu);
 }
 
 // x = r * 2^-e in fp32: one multiply, or two when 2^-e exceeds the float range
@@ -284,9 +291,9 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, co
                                                                     bool upd) {
   const float x = scale_down<BIG>(r, lv);
   if constexpr (SK == OZ_I8) {
-    const float y = rna_magic(x);
-    if (upd) r = __fmaf_rn(-__fsub_rn(y, kMagicF), lv.scale, r);   // exact
-    return (int8_t)(__float_as_uint(y) & 0xFFu);
+    const float q = round_q<true>(x);
+    if (upd) r = __fmaf_rn(-q, lv.scale, r);   // exact
+    return q_byte(q);
   } else {
     const auto q = slice_from_f32<SK>(x);
     if (upd) r = __fmaf_rn(-slice_to_f32<SK>(q), lv.scale, r);
@@ -295,18 +302,15 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, co
 }
 
 // every level of a non-fp64 input (fp32 residual, fp32 reference arithmetic):
-// trunc(fl32(x +- 0.5)) = sign(x) * floor(fl32(|x| + 0.5)), which is rounding
-// half away from zero except for |x| = 0.5 - 2^-25, where fl32(|x| + 0.5)
-// rounds up to 1 (checked exhaustively over every fp32 value below 512)
+// trunc(fl32(x +- 0.5)) = sign(x) * floor(fl32(|x| + 0.5))
 template <int SK, bool BIG>
 __device__ __forceinline__ typename SliceT<SK>::type step_f32_rd(float &r, const LevelP &lv,
                                                                  bool upd) {
   const float x = scale_down<BIG>(r, lv);   // == r / scale, rounded once
   if constexpr (SK == OZ_I8) {
-    float y = rna_magic(x);
-    if (fabsf(x) == __int_as_float(0x3EFFFFFF)) y = kMagicF + copysignf(1.0f, x);
-    if (upd) r = __fsub_rn(r, __fmul_rn(__fsub_rn(y, kMagicF), lv.scale));
-    return (int8_t)(__float_as_uint(y) & 0xFFu);
+    const float q = round_q<false>(x);
+    if (upd) r = __fsub_rn(r, __fmul_rn(q, lv.scale));
+    return q_byte(q);
   } else {
     const auto q = slice_from_f32<SK>(x);
     if (upd) r = __fsub_rn(r, __fmul_rn(slice_to_f32<SK>(q), lv.scale));
