@@ -203,9 +203,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-dgemm", action="store_true")
     ap.add_argument("--root-discount", type=int, default=768,
-                    help="multi-GPU: rows of A moved off rank 0, which also splits B")
+                    help="multi-GPU root mode: rows of A moved off rank 0, which also splits B")
     ap.add_argument("--chunks", type=int, default=0,
-                    help="multi-GPU: column blocks B is broadcast in (0 = by GPU count)")
+                    help="multi-GPU root mode: column blocks B is split and broadcast in "
+                         "(0 = auto)")
+    ap.add_argument("--dist", default="sharded", choices=["sharded", "root"],
+                    help="multi-GPU data layout: A rows x B column panels with an all-gather "
+                         "of B's slices (sharded), or B on rank 0 broadcast (root)")
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS),
                     help="benchmark configuration (C3 = the headline)")
     ap.add_argument("--num-splits", type=int, default=0, help="override the config's s")

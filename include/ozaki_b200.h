@@ -159,6 +159,27 @@ int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_sca
                   int64_t b_batches, void *c, int64_t ldc, uint32_t flags, void *stream);
 
 /*
+ * oz_cross_gemm with B's slices stored in column blocks (no counterpart in the
+ * reference, which has no multi-GPU path; this is the layout an all-gather or
+ * a blockwise broadcast of B's slices produces without a re-layout copy).
+ *
+ *   b_slices : (b_batches, blocks, num_splits, b_block_cols, ld), blocks =
+ *              ceil(n / b_block_cols); column c of B lives in block
+ *              c / b_block_cols at row c % b_block_cols (rows of the last
+ *              block past n are never read into stored outputs).
+ *   b_scales : (b_batches, blocks, num_splits, b_block_cols).
+ *   b_block_cols : a multiple of 128, or >= n (one block whose rows past n
+ *              are padding), or 0 for the plain layout of oz_cross_gemm.
+ * All other arguments as oz_cross_gemm; results are bit-identical to it.
+ */
+int oz_cross_gemm_blocked(const void *a_slices, const void *b_slices, const float *a_scales,
+                          const float *b_scales, int64_t batch, int64_t m, int64_t n, int64_t k,
+                          int64_t ld, int32_t num_splits, int slice_dtype, int out_dtype,
+                          const int32_t *a_index, const int32_t *b_index, int64_t a_batches,
+                          int64_t b_batches, int64_t b_block_cols, void *c, int64_t ldc,
+                          uint32_t flags, void *stream);
+
+/*
  * Device-side status: the kernels bound every spin-wait; when a bound is hit
  * they record a code in a device flag and return early (their output is then
  * undefined).  This call synchronises `stream`, returns OZ_OK or

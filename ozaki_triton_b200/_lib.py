@@ -38,6 +38,8 @@ SIGNATURES = {
     "oz_split_noalloc_max_bytes": (_i64, []),
     "oz_cross_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int, _int,
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
+    "oz_cross_gemm_blocked": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int,
+                                     _int, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),
     "oz_last_error": (ctypes.c_char_p, []),
     "oz_version": (ctypes.c_char_p, []),

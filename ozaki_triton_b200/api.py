@@ -111,13 +111,21 @@ def _check_cuda(*ts: torch.Tensor) -> None:
 
 
 def _split_lines(x3: torch.Tensor, stride_line: int, stride_k: int, lines: int, k: int,
-                 num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int
+                 num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int,
+                 out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
                  ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Split the lines of a (batch, ., .) view; returns padded slices + scales."""
+    """Split the lines of a (batch, ., .) view; returns padded slices + scales
+    (written into ``out`` = contiguous (slices, scales) of that shape if given)."""
     batch = x3.shape[0]
     ld = slice_row_elems(k, slice_dtype)
-    slices = torch.empty((batch, num_splits, lines, ld), dtype=slice_dtype, device=x3.device)
-    scales = torch.empty((batch, num_splits, lines), dtype=torch.float32, device=x3.device)
+    if out is not None:
+        slices, scales = out
+        assert slices.shape == (batch, num_splits, lines, ld) and slices.is_contiguous()
+        assert scales.shape == (batch, num_splits, lines) and scales.is_contiguous()
+        assert slices.dtype == slice_dtype and scales.dtype == torch.float32
+    else:
+        slices = torch.empty((batch, num_splits, lines, ld), dtype=slice_dtype, device=x3.device)
+        scales = torch.empty((batch, num_splits, lines), dtype=torch.float32, device=x3.device)
     if batch == 0 or lines == 0:
         return slices, scales
     lib = _lib.load()

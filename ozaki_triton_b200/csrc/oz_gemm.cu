@@ -54,6 +54,8 @@ struct GemmParams {
   int skip_tail;
   int batch;
   int tiles_m, tiles_n, num_tiles;
+  int gm;                // row tiles per raster group
+  int bw, bblocks;       // B stored in column blocks of bw columns (bblocks per batch)
   int stages;            // pipeline depth
   uint32_t idesc;        // instruction descriptor without the N field
 };
@@ -96,7 +98,7 @@ __device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, 
   const int tpb = p.tiles_m * p.tiles_n;
   b = t / tpb;
   int local = t - b * tpb;
-  constexpr int GM = 16;
+  const int GM = p.gm;
   int per_group = GM * p.tiles_n;
   int group = local / per_group;
   int first_m = group * GM;
@@ -202,7 +204,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int ai = p.a_index ? p.a_index[b] : b;
         const int bi = p.b_index ? p.b_index[b] : b;
         const int arow = mb * TM + (int)rank * kBM;
-        const int brow = nb * NT + (int)rank * R;
+        // B column blocks: a tile never straddles two (bw is a multiple of NT)
+        const int blk = (nb * NT) / p.bw;
+        const int brow = nb * NT - blk * p.bw + (int)rank * R;
+        const int bz = (bi * p.bblocks + blk) * s;
         for (int i = 0; ok && i < s; ++i) {
           for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
             const int slot = it % S;
@@ -214,11 +219,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (leader) mbar_arrive_expect_tx(&full[slot], tx);
               const uint32_t fb = leader_addr(&full[slot]);
               tma_load_3d_pair(st, &tm_a, fb, kb * kKBytes, arow, ai * s + i);
-              tma_load_3d_pair(st + a_tile_bytes(), &tm_b, fb, kb * kKBytes, brow, bi * s);
+              tma_load_3d_pair(st + a_tile_bytes(), &tm_b, fb, kb * kKBytes, brow, bz);
             } else {
               mbar_arrive_expect_tx(&full[slot], tx);
               tma_load_3d(st, &tm_a, &full[slot], kb * kKBytes, arow, ai * s + i);
-              tma_load_3d(st + a_tile_bytes(), &tm_b, &full[slot], kb * kKBytes, brow, bi * s);
+              tma_load_3d(st + a_tile_bytes(), &tm_b, &full[slot], kb * kKBytes, brow, bz);
             }
           }
         }
@@ -309,6 +314,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int bi = p.b_index ? p.b_index[b] : b;
       const int m = mb * TM + row;
       const int n0 = nb * NT + half * NH;
+      const int blk = (nb * NT) / p.bw;
       for (int i = 0; i < s; ++i, ++pass) {
         const int js = p.skip_tail ? s - i : s;
         const int buf = pass % nbuf;
@@ -320,7 +326,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         for (int j = 0; j < js; ++j) {
-          const float *sbp = p.b_scales + ((int64_t)bi * s + j) * p.n;
+          // scales of B slice j in this tile's column block, indexed by global column
+          const float *sbp = p.b_scales + (((int64_t)bi * p.bblocks + blk) * s + j) * p.bw -
+                             (int64_t)blk * p.bw;
           const int g = j / SPG, jj = j % SPG;
           int col;
           if constexpr (PAIR == 2) {
@@ -511,13 +519,15 @@ int status_gemm(int *value, bool clear) { return read_status_word(value, clear);
 
 }  // namespace oz
 
-extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_scales,
-                             const float *b_scales, int64_t batch, int64_t m, int64_t n,
-                             int64_t k, int64_t ld, int32_t num_splits, int slice_dtype,
-                             int out_dtype, const int32_t *a_index, const int32_t *b_index,
-                             int64_t a_batches, int64_t b_batches, void *c, int64_t ldc,
-                             uint32_t flags, void *stream) {
-  using namespace oz;
+namespace oz {
+namespace {
+
+int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_scales,
+                    const float *b_scales, int64_t batch, int64_t m, int64_t n, int64_t k,
+                    int64_t ld, int32_t num_splits, int slice_dtype, int out_dtype,
+                    const int32_t *a_index, const int32_t *b_index, int64_t a_batches,
+                    int64_t b_batches, int64_t b_block_cols, void *c, int64_t ldc,
+                    uint32_t flags, void *stream) {
   if (num_splits < 1 || num_splits > 8)
     return set_error(OZ_ERR_INVALID, "num_splits must be in [1, 8], got %d", num_splits);
   if (batch < 0 || m < 0 || n < 0 || k < 0)
@@ -528,6 +538,10 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
   if (out_dtype != OZ_F64 && out_dtype != OZ_F32 && out_dtype != OZ_F16 && out_dtype != OZ_BF16)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported output dtype %d", out_dtype);
   if (flags & ~OZ_GEMM_SKIP_TAIL) return set_error(OZ_ERR_INVALID, "unknown flags 0x%x", flags);
+  if (b_block_cols < 0 || (b_block_cols > 0 && b_block_cols < n && b_block_cols % 128 != 0))
+    return set_error(OZ_ERR_INVALID,
+                     "B column block width must be 0, >= n or a multiple of 128 (got %lld)",
+                     (long long)b_block_cols);
   if (batch == 0 || m == 0 || n == 0) return OZ_OK;
   if (!c || ldc < n) return set_error(OZ_ERR_INVALID, "bad output (ldc=%lld n=%lld)",
                                       (long long)ldc, (long long)n);
@@ -552,8 +566,10 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
   if (a_batches < 1 || b_batches < 1 || (!a_index && a_batches < batch) ||
       (!b_index && b_batches < batch))
     return set_error(OZ_ERR_INVALID, "bad operand batch counts");
-  if (m > INT32_MAX || n > INT32_MAX || a_batches * num_splits > INT32_MAX ||
-      b_batches * num_splits > INT32_MAX)
+  const int64_t bw = b_block_cols == 0 ? n : b_block_cols;
+  const int64_t bblocks = (n + bw - 1) / bw;
+  if (m > INT32_MAX || n > INT32_MAX || bw > INT32_MAX || a_batches * num_splits > INT32_MAX ||
+      b_batches * bblocks * num_splits > INT32_MAX)
     return set_error(OZ_ERR_INVALID, "size out of range");
 
   const TileChoice tc = choose_tile(m, num_splits);
@@ -563,8 +579,9 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
                         (uint64_t)(a_batches * num_splits), kBM, 1))
     return rc;
   // B: one box = the K block of all num_splits slices, stacked
-  if (int rc = make_map(&tb, b_slices, (uint64_t)ld_bytes, (uint64_t)n,
-                        (uint64_t)(b_batches * num_splits), (uint32_t)(nt / pair),
+  // (column blocks: the slices of block c of batch b are matrices (b*blocks + c)*s + j)
+  if (int rc = make_map(&tb, b_slices, (uint64_t)ld_bytes, (uint64_t)bw,
+                        (uint64_t)(b_batches * bblocks * num_splits), (uint32_t)(nt / pair),
                         (uint32_t)num_splits))
     return rc;
 
@@ -583,6 +600,13 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
   p.batch = (int)batch;
   p.tiles_m = (int)((m + kBM * pair - 1) / (kBM * pair));
   p.tiles_n = (int)((n + nt - 1) / nt);
+  p.bw = (int)bw;
+  p.bblocks = (int)bblocks;
+  p.gm = 16;
+  if (const char *env = getenv("OZ_GEMM_GM")) {
+    const int g = atoi(env);
+    if (g >= 1 && g <= 64) p.gm = g;
+  }
   int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
@@ -596,4 +620,30 @@ extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const f
   }
   if (nt == 128) return launch_kind<128, 1>(kind, out_dtype, ta, tb, p, st);
   return launch_kind<64, 1>(kind, out_dtype, ta, tb, p, st);
+}
+
+}  // namespace
+}  // namespace oz
+
+extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_scales,
+                             const float *b_scales, int64_t batch, int64_t m, int64_t n,
+                             int64_t k, int64_t ld, int32_t num_splits, int slice_dtype,
+                             int out_dtype, const int32_t *a_index, const int32_t *b_index,
+                             int64_t a_batches, int64_t b_batches, void *c, int64_t ldc,
+                             uint32_t flags, void *stream) {
+  return oz::cross_gemm_impl(a_slices, b_slices, a_scales, b_scales, batch, m, n, k, ld,
+                             num_splits, slice_dtype, out_dtype, a_index, b_index, a_batches,
+                             b_batches, 0, c, ldc, flags, stream);
+}
+
+extern "C" int oz_cross_gemm_blocked(const void *a_slices, const void *b_slices,
+                                     const float *a_scales, const float *b_scales, int64_t batch,
+                                     int64_t m, int64_t n, int64_t k, int64_t ld,
+                                     int32_t num_splits, int slice_dtype, int out_dtype,
+                                     const int32_t *a_index, const int32_t *b_index,
+                                     int64_t a_batches, int64_t b_batches, int64_t b_block_cols,
+                                     void *c, int64_t ldc, uint32_t flags, void *stream) {
+  return oz::cross_gemm_impl(a_slices, b_slices, a_scales, b_scales, batch, m, n, k, ld,
+                             num_splits, slice_dtype, out_dtype, a_index, b_index, a_batches,
+                             b_batches, b_block_cols, c, ldc, flags, stream);
 }

@@ -7,10 +7,13 @@ every B column is split independently (per-row / per-column scales), so a
 shard's slices are bit-identical to the corresponding rows of the global
 split:
 
+* ``ozaki_matmul_sharded``: A sharded by rows and B by column panels; each
+  rank splits only its own rows and its own panel, and one all-gather moves
+  the panels' slices (for int8 slices half the bytes of the fp64 panels) to
+  every rank while the A rows are split; every rank computes its rows of C.
 * ``ozaki_matmul_mrows``: A sharded by row blocks; B lives on one root rank,
-  which splits it once and broadcasts its slices and scales (for int8 slices
-  half the bytes of the fp64 B); every rank computes its rows of C.  The
-  broadcast runs while each rank splits its own A rows.
+  which splits it in column blocks and broadcasts each block's slices and
+  scales while it splits the next; every rank computes its rows of C.
 * ``ozaki_matmul_batches``: the broadcast batch of a batched matmul is cut in
   contiguous ranges of output batches; each rank computes its range from the
   operand members that range references (no exchange at all).
@@ -52,25 +55,28 @@ class Backend:
     """Device compute used by the sharded drivers (the CUDA library)."""
 
     def split(self, x3: torch.Tensor, stride_line: int, stride_k: int, lines: int, k: int,
-              num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int):
+              num_splits: int, alpha: int, slice_dtype: torch.dtype, mode: int, out=None):
         return _split_lines(x3, stride_line, stride_k, lines, k, num_splits, alpha,
-                            slice_dtype, mode)
+                            slice_dtype, mode, out=out)
 
     def gemm(self, a_sl, b_sl, a_sc, b_sc, batch: int, m: int, n: int, k: int, num_splits: int,
              out_dtype: torch.dtype, skip_tail: bool, a_idx=None, b_idx=None,
-             out: Optional[torch.Tensor] = None, col0: int = 0) -> torch.Tensor:
+             out: Optional[torch.Tensor] = None, col0: int = 0,
+             b_block_cols: int = 0) -> torch.Tensor:
         """C (batch, m, n); with ``out`` (batch, m, N_total) the result is written
-        into its columns [col0, col0 + n) instead."""
+        into its columns [col0, col0 + n) instead.  With ``b_block_cols`` the B
+        slices are (BB, blocks, s, b_block_cols, ld) and their scales
+        (BB, blocks, s, b_block_cols): column blocks as a gather produces them."""
         c = torch.empty((batch, m, n), dtype=out_dtype, device=a_sl.device) if out is None else out
         if batch == 0 or m == 0 or n == 0:
             return c
         ptr = c.data_ptr() + col0 * c.element_size()
-        _lib.check(_lib.load().oz_cross_gemm(
+        _lib.check(_lib.load().oz_cross_gemm_blocked(
             a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), batch, m, n, k,
             a_sl.shape[-1], num_splits, _OZ_DTYPE[a_sl.dtype], _OZ_DTYPE[out_dtype],
             a_idx.data_ptr() if a_idx is not None else None,
             b_idx.data_ptr() if b_idx is not None else None, a_sl.shape[0], b_sl.shape[0],
-            ptr, c.stride(-2), _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+            b_block_cols, ptr, c.stride(-2), _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
             torch.cuda.current_stream(a_sl.device).cuda_stream))
         return c
 
@@ -110,10 +116,51 @@ def weighted_rows(m: int, world: int, root: int = 0, root_discount: int = 0,
     return rows
 
 
+def block_width(n: int, parts: int, align: int = 128) -> int:
+    """Width of the column blocks B's slices travel in: n in ``parts`` blocks
+    of a multiple of ``align`` columns (the GEMM's tile width), the last one
+    possibly narrower.  One block (width n) for parts <= 1."""
+    if parts <= 1 or n <= align:
+        return n
+    return -(-n // (parts * align)) * align
+
+
+def column_panel(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """[start, stop) of the B columns rank ``rank`` holds in ``ozaki_matmul_sharded``:
+    blocks of ``block_width(n, world)`` columns, trailing ranks possibly empty."""
+    w = block_width(n, world)
+    return min(n, rank * w), min(n, (rank + 1) * w)
+
+
+def _blocked_buffers(blocks: int, num_splits: int, w: int, ld: int, slice_dtype, dev):
+    sl = torch.empty((1, blocks, num_splits, w, ld), dtype=slice_dtype, device=dev)
+    sc = torch.empty((1, blocks, num_splits, w), dtype=torch.float32, device=dev)
+    return sl, sc
+
+
+def _split_block(backend, Bc: torch.Tensor, k: int, num_splits: int, alpha: int, slice_dtype,
+                 mode: int, sl_block: torch.Tensor, sc_block: torch.Tensor):
+    """Split the columns of Bc (k, nc) into one block (s, w, ld) / (s, w) of the
+    gather buffers; nc <= w (a narrower block leaves its last rows unused)."""
+    nc = Bc.shape[1]
+    w = sl_block.shape[1]
+    if nc == 0:
+        return
+    B3 = Bc.reshape(1, k, nc)
+    if nc == w:
+        backend.split(B3, B3.stride(2), B3.stride(1), nc, k, num_splits, alpha, slice_dtype,
+                      mode, out=(sl_block.unsqueeze(0), sc_block.unsqueeze(0)))
+    else:
+        t_sl, t_sc = backend.split(B3, B3.stride(2), B3.stride(1), nc, k, num_splits, alpha,
+                                   slice_dtype, mode)
+        sl_block[:, :nc].copy_(t_sl[0])
+        sc_block[:, :nc].copy_(t_sc[0])
+
+
 def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_splits: int = 3,
                        slice_dtype: torch.dtype = torch.float16, *, root: int = 0,
                        group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
-                       chunks: Optional[int] = None,
+                       b_blocks: Optional[int] = None,
                        backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B, A sharded by rows, B on ``root`` only.
 
@@ -122,15 +169,17 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
     Returns this rank's rows of C (M_local, N) in the input dtype, equal bit
     for bit to the same rows of the single-GPU ``ozaki_matmul``.
 
-    B travels in ``chunks`` column blocks (multiples of 256 columns): the root
-    splits block c and starts its broadcast before splitting block c + 1, and
-    every rank starts the GEMM of block c as soon as it has arrived.
+    The root splits B in ``b_blocks`` column blocks and broadcasts each block's
+    slices as soon as it is split, so the broadcast of block c overlaps the
+    split of block c + 1.  The blocks land in place in a column-blocked slice
+    buffer that the GEMM reads directly (one launch over all of N).
     """
     backend = backend or Backend()
     dev = A_local.device
     _check_args(A_local.dtype, num_splits, slice_dtype)
     m_loc, k = A_local.shape
     rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
     # the root announces N (and checks K); every rank takes the same steps
     shape = torch.tensor([B.shape[0], B.shape[1]] if rank == root else [0, 0],
                          dtype=torch.int64, device=dev)
@@ -141,37 +190,89 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
                                dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
     mode = _residual_mode(residual, num_splits, A_local.dtype)
     ld = _lib_row(k, slice_dtype)
-    if chunks is None:
-        chunks = 1
-    blocks = (n + 255) // 256
-    chunks = max(1, min(chunks, blocks))
-    bounds = []
-    for c in range(chunks):
-        b0, b1 = block_range(blocks, chunks, c)
-        bounds.append((b0 * 256, min(n, b1 * 256)))
-    pieces, works = [], []
-    for c0, c1 in bounds:
-        nc = c1 - c0
+    if b_blocks is None:
+        b_blocks = 4 if (world > 1 and n >= 4096) else 1
+    w = block_width(n, b_blocks)
+    blocks = -(-n // w) if n > 0 else 0
+    b_sl, b_sc = _blocked_buffers(blocks, num_splits, w, ld, slice_dtype, dev)
+    works = []
+    for c in range(blocks):
         if rank == root:
-            Bc = B[:, c0:c1].reshape(1, k, nc)
-            b_sl, b_sc = backend.split(Bc, Bc.stride(2), Bc.stride(1), nc, k, num_splits, alpha,
-                                       slice_dtype, mode)
-        else:
-            b_sl = torch.empty((1, num_splits, nc, ld), dtype=slice_dtype, device=dev)
-            b_sc = torch.empty((1, num_splits, nc), dtype=torch.float32, device=dev)
-        works.append((dist.broadcast(b_sl, src=root, group=group, async_op=True),
-                      dist.broadcast(b_sc, src=root, group=group, async_op=True)))
-        pieces.append((b_sl, b_sc))
+            _split_block(backend, B[:, c * w:min(n, (c + 1) * w)], k, num_splits, alpha,
+                         slice_dtype, mode, b_sl[0, c], b_sc[0, c])
+        works.append(dist.broadcast(b_sl[0, c], src=root, group=group, async_op=True))
+        works.append(dist.broadcast(b_sc[0, c], src=root, group=group, async_op=True))
     # this rank's rows of A are split while the blocks of B travel
     A3 = A_local.reshape(1, m_loc, k)
     a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
                                slice_dtype, mode)
-    c = torch.empty((1, m_loc, n), dtype=A_local.dtype, device=dev)
-    for (c0, c1), (b_sl, b_sc), (w1, w2) in zip(bounds, pieces, works):
-        w1.wait()
-        w2.wait()
-        backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, c1 - c0, k, num_splits, A_local.dtype,
-                     skip_tail, out=c, col0=c0)
+    for wk in works:
+        wk.wait()
+    c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
+                     skip_tail, b_block_cols=w)
+    return c.reshape(m_loc, n)
+
+
+def _all_gather_inplace(buf: torch.Tensor, rank: int, group, async_op: bool):
+    """All-gather of buf[0, r] from every rank r into buf (1, world, ...)."""
+    if dist.get_backend(group) == "nccl":
+        return dist.all_gather_into_tensor(buf.view(-1), buf[0, rank].reshape(-1), group=group,
+                                           async_op=async_op)
+    parts = [buf[0, r] for r in range(buf.shape[1])]
+    return dist.all_gather(parts, buf[0, rank].clone(), group=group, async_op=async_op)
+
+
+def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_splits: int = 3,
+                         slice_dtype: torch.dtype = torch.float16, *, n: Optional[int] = None,
+                         group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
+                         backend: Optional[Backend] = None) -> torch.Tensor:
+    """C_local = A_local @ B with A sharded by rows and B by column panels.
+
+    Rank r passes its rows of A (M_local, K) (any split of the rows) and its
+    panel of B's columns (K, N_r), the columns ``column_panel(N, world, r)``;
+    ``n`` (N) may be given to save one small collective.  Each rank splits
+    only its own panel and its own rows; one all-gather then moves the int8
+    (or float) slices of every panel to every rank -- for int8 slices half the
+    bytes of the fp64 panels -- into a column-blocked buffer that the GEMM
+    reads in place.  The split of A's rows overlaps the all-gather.  Returns
+    this rank's rows of C (M_local, N), bit-identical to the same rows of the
+    single-GPU ``ozaki_matmul``.
+    """
+    backend = backend or Backend()
+    dev = A_local.device
+    _check_args(A_local.dtype, num_splits, slice_dtype)
+    assert A_local.dtype == B_local.dtype
+    m_loc, k = A_local.shape
+    assert B_local.shape[0] == k, f"contraction dim mismatch: {A_local.shape} @ {B_local.shape}"
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    if n is None:
+        t = torch.tensor([B_local.shape[1]], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, group=group)
+        n = int(t.item())
+    c0, c1 = column_panel(n, world, rank)
+    assert B_local.shape[1] == c1 - c0, \
+        f"rank {rank} holds {B_local.shape[1]} columns of B, expected {c1 - c0} ({c0}:{c1})"
+    alpha = compute_split_bits(k, slice_dtype=slice_dtype,
+                               dot_accum_dtype=select_dot_accum_dtype(slice_dtype))
+    mode = _residual_mode(residual, num_splits, A_local.dtype)
+    ld = _lib_row(k, slice_dtype)
+    w = block_width(n, world)
+    if world == 1 or n == 0:
+        w = max(n, 1)
+    # one block per rank (blocks past ceil(n / w) stay empty and are not read)
+    b_sl, b_sc = _blocked_buffers(world, num_splits, w, ld, slice_dtype, dev)
+    _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, b_sl[0, rank],
+                 b_sc[0, rank])
+    works = [_all_gather_inplace(b_sl, rank, group, True),
+             _all_gather_inplace(b_sc, rank, group, True)]
+    A3 = A_local.reshape(1, m_loc, k)
+    a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
+                               slice_dtype, mode)
+    for wk in works:
+        wk.wait()
+    c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
+                     skip_tail, b_block_cols=w)
     return c.reshape(m_loc, n)
 
 

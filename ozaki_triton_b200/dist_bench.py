@@ -1,9 +1,12 @@
 """bench.py's multi-GPU leg (one process per GPU under torchrun).
 
 Headline workload (config C3): FP64 -> INT8, num_splits = 4, M = N = K = 8192.
-A is sharded by row blocks across the ranks; B lives on rank 0, which splits
-it and broadcasts the slices + scales over NCCL (``dist.ozaki_matmul_mrows``).
-Total work is fixed: strong scaling.  The step time is the max over ranks of
+Default layout (``--dist sharded``): A sharded by row blocks and B by column
+panels; every rank splits its own rows and panel and the panels' int8 slices
+are all-gathered over NCCL (``dist.ozaki_matmul_sharded``).  ``--dist root``:
+B lives on rank 0, which splits it in column blocks and broadcasts each
+block's slices (``dist.ozaki_matmul_mrows``).  Total work is fixed: strong
+scaling.  The step time is the max over ranks of
 each rank's CUDA-event time, with a barrier and a device synchronise on both
 sides of the timed region.
 """
@@ -31,14 +34,20 @@ def main(args):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     M, N, K, S = bench.M, bench.N, bench.K, bench.NUM_SPLITS
-    # rank 0 also splits and broadcasts B: it takes fewer rows of A (about the
-    # rows its B split is worth at this problem's per-row GEMM rate)
-    rows = ozd.weighted_rows(M, world, root=0, root_discount=int(args.root_discount))
+    sharded = args.dist == "sharded"
+    if sharded:
+        rows = [b - a for a, b in (ozd.block_range(M, world, r) for r in range(world))]
+        p0, p1 = ozd.column_panel(N, world, rank)
+    else:
+        # rank 0 also splits and broadcasts B: it takes fewer rows of A (about
+        # the rows its B split is worth at this problem's per-row GEMM rate)
+        rows = ozd.weighted_rows(M, world, root=0, root_discount=int(args.root_discount))
+        p0, p1 = (0, N) if rank == 0 else (0, 0)
     lo = sum(rows[:rank])
     hi = lo + rows[rank]
     a_h, b_h = bench.make_inputs()
     a_loc = a_h[lo:hi].contiguous().to(dev)
-    b = b_h.to(dev) if rank == 0 else None
+    b = b_h[:, p0:p1].contiguous().to(dev) if (sharded or rank == 0) else None
     stream = torch.cuda.current_stream()
     gemm_ms = []
 
@@ -58,12 +67,17 @@ def main(args):
 
     be = TimedBackend()
 
-    # one block: at 8192^3 each rank's GEMM over a fraction of N no longer
-    # fills the GPU (measured: 2 blocks 562, 1 block 607 TFLOPS on 8 GPUs)
-    chunks = args.chunks or 1
+    # root mode: B travels in column blocks (split of block c+1 overlaps the
+    # broadcast of block c); one GEMM over all of N once B is complete
+    b_blocks = args.chunks or None
+
+    def run(a_dev, b_dev):
+        if sharded:
+            return ozd.ozaki_matmul_sharded(a_dev, b_dev, S, torch.int8, n=N, backend=be)
+        return ozd.ozaki_matmul_mrows(a_dev, b_dev, S, torch.int8, backend=be, b_blocks=b_blocks)
 
     def step():
-        return ozd.ozaki_matmul_mrows(a_loc, b, S, torch.int8, backend=be, chunks=chunks)
+        return run(a_loc, b)
 
     for _ in range(args.warmup):
         step()
@@ -90,14 +104,14 @@ def main(args):
     e2e = None
     if not args.no_e2e:
         a_pin = a_h[lo:hi].contiguous().pin_memory()
-        b_pin = b_h.pin_memory() if rank == 0 else None
+        b_pin = b_h[:, p0:p1].contiguous().pin_memory() if (sharded or rank == 0) else None
         c_pin = torch.empty((hi - lo, N), dtype=torch.float64).pin_memory()
         be.record = False
 
         def e2e_step():
             ad = a_pin.to(dev, non_blocking=True)
-            bd = b_pin.to(dev, non_blocking=True) if rank == 0 else None
-            cd = ozd.ozaki_matmul_mrows(ad, bd, S, torch.int8, backend=be, chunks=chunks)
+            bd = b_pin.to(dev, non_blocking=True) if b_pin is not None else None
+            cd = run(ad, bd)
             c_pin.copy_(cd, non_blocking=True)
 
         for _ in range(2):
@@ -116,7 +130,7 @@ def main(args):
         te = torch.tensor([s0.elapsed_time(s1) / n_e2e], dtype=torch.float64, device=dev)
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te.item())
-        h2d = (hi - lo) * K * 8 + (K * N * 8 if rank == 0 else 0)
+        h2d = (hi - lo) * K * 8 + K * (p1 - p0) * 8
         e2e = {"value": 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": M * K * 8 + K * N * 8,
                "d2h_bytes_per_step": M * N * 8, "h2d_bytes_rank": h2d}
@@ -133,16 +147,22 @@ def main(args):
             "config": {"workload": bench.WORKLOAD, "M": M, "N": N, "K": K, "num_splits": S,
                        "slice_dtype": "int8", "input_dtype": "fp64", "residual": "compat",
                        "l2": "no flush: operands larger than the 126 MB L2",
-                       "parallelism": f"M-row sharding over {world} GPUs, B slices "
-                                      "broadcast from rank 0 over NCCL in column blocks",
-                       "rows_per_rank": rows, "b_blocks": chunks},
+                       "parallelism": (f"A rows x B column panels over {world} GPUs, B "
+                                       "slices all-gathered over NCCL" if sharded else
+                                       f"M-row sharding over {world} GPUs, B slices broadcast "
+                                       "from rank 0 over NCCL in column blocks"),
+                       "rows_per_rank": rows,
+                       "b_panel_cols": ozd.block_width(N, world) if sharded else None,
+                       "b_blocks": None if sharded else (b_blocks or "auto")},
             "roofline": {"bound": "tensor", "kernel": "cross_gemm_kernel (rank 0 rows)",
                          "achieved": achieved, "peak": 2.0 * bf16_peak, "unit": "TFLOP/s",
                          "frac": achieved / (2.0 * bf16_peak),
                          "peak_source": f"2x {peak_src} dense bf16; B200 dense int8 = 2x bf16",
                          "gemm_ms": g_local, "traffic": None},
             "clocks": clk.summary(),
-            "gpu_launches": (4 + 2 * (world - 1)) * args.steps,
+            # rank 0's own kernels per step: transpose + split of B's panel (or
+            # blocks), split of A's rows, the GEMM (NCCL kernels not counted)
+            "gpu_launches": (4 if sharded else 2 + 2 * (b_blocks or 4)) * args.steps,
             "e2e": e2e,
         }
         print(json.dumps(line), flush=True)

@@ -30,18 +30,28 @@ class OracleBackend:
     def __init__(self, residual="compat"):
         self.residual = residual
 
-    def split(self, x3, stride_line, stride_k, lines, k, s, alpha, slice_dtype, mode):
+    def split(self, x3, stride_line, stride_k, lines, k, s, alpha, slice_dtype, mode, out=None):
         x = torch.as_strided(x3, (x3.shape[0], lines, k), (x3.stride(0), stride_line, stride_k))
         sl, sc = oracle.split_lines(x.numpy(), s, alpha, KIND[slice_dtype], KIND[x3.dtype],
                                     residual="compat" if mode == 0 else "exact")
         ld = ozd._lib_row(k, slice_dtype)
-        out = torch.zeros((x3.shape[0], s, lines, ld), dtype=slice_dtype)
-        out[..., :k] = torch.from_numpy(sl.astype(np.float32) if slice_dtype != torch.int8 else sl
-                                        ).to(slice_dtype)
-        return out, torch.from_numpy(sc)
+        if out is None:
+            out = (torch.empty((x3.shape[0], s, lines, ld), dtype=slice_dtype),
+                   torch.empty((x3.shape[0], s, lines), dtype=torch.float32))
+        o_sl, o_sc = out
+        o_sl.zero_()
+        o_sl[..., :k] = torch.from_numpy(sl.astype(np.float32) if slice_dtype != torch.int8 else sl
+                                         ).to(slice_dtype)
+        o_sc.copy_(torch.from_numpy(sc))
+        return o_sl, o_sc
 
     def gemm(self, a_sl, b_sl, a_sc, b_sc, batch, m, n, k, s, out_dtype, skip_tail,
-             a_idx=None, b_idx=None, out=None, col0=0):
+             a_idx=None, b_idx=None, out=None, col0=0, b_block_cols=0):
+        if b_block_cols:
+            # column blocks (BB, blocks, s, w, ld) -> plain (BB, s, n, ld)
+            bb, blocks, _, w, ld = b_sl.shape
+            b_sl = b_sl.permute(0, 2, 1, 3, 4).reshape(bb, s, blocks * w, ld)[:, :, :n]
+            b_sc = b_sc.permute(0, 2, 1, 3).reshape(bb, s, blocks * w)[:, :, :n]
         ai = a_idx.long() if a_idx is not None else torch.arange(batch)
         bi = b_idx.long() if b_idx is not None else torch.arange(batch)
         a = a_sl[ai, ..., :k].numpy()
@@ -101,11 +111,23 @@ def case_mrows(rank, world, out_dir):
     c = ozd.ozaki_matmul_mrows(A[lo:hi], B if rank == 0 else None, 4, torch.int8,
                                backend=OracleBackend())
     np.save(os.path.join(out_dir, f"c{rank}.npy"), c.numpy())
-    # the same through three broadcast blocks of B's columns
+    # the same through three broadcast blocks of B's columns (256, 256, 88)
     B2 = law(g, (64, 600))
-    c2 = ozd.ozaki_matmul_mrows(A[lo:hi], B2 if rank == 0 else None, 4, torch.int8, chunks=3,
-                                backend=OracleBackend())
+    c2 = ozd.ozaki_matmul_mrows(A[lo:hi], B2 if rank == 0 else None, 4, torch.int8,
+                                b_blocks=3, backend=OracleBackend())
     np.save(os.path.join(out_dir, f"d{rank}.npy"), c2.numpy())
+
+
+def case_sharded(rank, world, out_dir):
+    g = torch.Generator().manual_seed(8)
+    A = law(g, (37, 64))
+    for name, n in (("a", 600), ("b", 100), ("c", 256)):
+        B = law(g, (64, n))
+        c0, c1 = ozd.column_panel(n, world, rank)
+        lo, hi = ozd.block_range(37, world, rank)
+        c = ozd.ozaki_matmul_sharded(A[lo:hi], B[:, c0:c1], 4, torch.int8,
+                                     n=None if name == "a" else n, backend=OracleBackend())
+        np.save(os.path.join(out_dir, f"{name}{rank}.npy"), c.numpy())
 
 
 def case_batches(rank, world, out_dir):
@@ -159,6 +181,32 @@ def test_mrows_two_ranks_bit_identical(tmp_path):
     B2 = law(g, (64, 600))
     d = np.concatenate([np.load(tmp_path / f"d{r}.npy") for r in range(2)])
     assert np.array_equal(d, oracle.ozaki_matmul(A.numpy(), B2.numpy(), 4, "int8", "fp64"))
+
+
+def test_sharded_two_ranks_bit_identical(tmp_path):
+    """A by rows, B by column panels (ragged last panel, an empty panel, exact
+    fit), slices all-gathered into the column-blocked buffer."""
+    codes = run_ranks(case_sharded, 2, tmp_path)
+    assert codes == [0, 0], [open(p).read() for p in tmp_path.glob("err*.txt")]
+    g = torch.Generator().manual_seed(8)
+    A = law(g, (37, 64))
+    for name, n in (("a", 600), ("b", 100), ("c", 256)):
+        B = law(g, (64, n))
+        got = np.concatenate([np.load(tmp_path / f"{name}{r}.npy") for r in range(2)])
+        assert np.array_equal(got, oracle.ozaki_matmul(A.numpy(), B.numpy(), 4, "int8", "fp64"))
+
+
+def test_column_panels_cover_n():
+    for n in [0, 1, 100, 128, 129, 600, 8192, 8193]:
+        for world in [1, 2, 3, 8]:
+            panels = [ozd.column_panel(n, world, r) for r in range(world)]
+            assert panels[0][0] == 0 and panels[-1][1] == n
+            w = ozd.block_width(n, world)
+            for r, (a, b) in enumerate(panels):
+                assert a <= b and (b - a) <= w
+                if b > a:
+                    assert a == r * w                 # block r of the gather buffer
+            assert w == n or w % 128 == 0
 
 
 def test_batches_two_ranks_cover_the_broadcast(tmp_path):

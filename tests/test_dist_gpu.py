@@ -1,6 +1,7 @@
 """Sharded paths on >= 2 GPUs with NCCL (one process per GPU): the
-M-row-sharded GEMM with the B broadcast, and batch sharding, give the same
-bits as the single-GPU call.  Skipped with fewer than two GPUs."""
+M-row-sharded GEMM with the B broadcast, rows x column panels with the
+all-gather, and batch sharding give the same bits as the single-GPU call.
+Skipped with fewer than two GPUs."""
 
 import os
 import socket
@@ -42,8 +43,15 @@ def _worker(rank, world, port, out_dir):
         want = oz.ozaki_matmul(A.to(dev), B.to(dev), 4, torch.int8)[lo:hi]
         ok1 = torch.equal(c, want)
         c3 = ozd.ozaki_matmul_mrows(A[lo:hi].to(dev), B.to(dev) if rank == 0 else None, 4,
-                                    torch.int8, chunks=2)
+                                    torch.int8, b_blocks=2)
         ok1 = ok1 and torch.equal(c3, want)
+        # A by rows, B by column panels, slices all-gathered
+        for n in (300, 1000):
+            Bn = (torch.rand(700, n, generator=g, dtype=torch.float64) - 0.5) * 3.0
+            p0, p1 = ozd.column_panel(n, world, rank)
+            cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4, torch.int8)
+            ok1 = ok1 and torch.equal(cs, oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4,
+                                                           torch.int8)[lo:hi])
         A4 = torch.randn(4, 1, 64, 96, generator=g, dtype=torch.float64)
         B4 = torch.randn(1, 3, 96, 40, generator=g, dtype=torch.float64)
         cb, s0, s1 = ozd.ozaki_matmul_batches(A4.to(dev), B4.to(dev), 3, torch.float16)

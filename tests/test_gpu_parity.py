@@ -314,6 +314,42 @@ def test_gemm_tile_configs_bit_identical(tile, s, monkeypatch):
     assert oz.device_status() == 0
 
 
+@pytest.mark.parametrize("n,w,sk,tile", [(1000, 256, "int8", "2,128"), (1000, 128, "int8", "1,64"),
+                                         (700, 128, "fp16", "2,128"), (300, 512, "int8", "2,128"),
+                                         (384, 384, "int8", "1,128"), (130, 128, "fp32", "2,64")])
+def test_gemm_column_blocked_b_bit_identical(n, w, sk, tile, monkeypatch):
+    """oz_cross_gemm_blocked (B's slices in column blocks, the layout of the
+    multi-GPU gather) gives the same bits as oz_cross_gemm on the plain layout,
+    with the unused rows of the last block (and their scales) holding garbage."""
+    from ozaki_triton_b200 import api
+    from ozaki_triton_b200 import dist as ozd
+    monkeypatch.setenv("OZ_GEMM_TILE", tile)
+    rng = np.random.default_rng(5)
+    M, K, s = 300, 520, 3
+    a = to_dev(rng.standard_normal((1, M, K)), "fp64")
+    b = to_dev(rng.standard_normal((1, K, n)), "fp64")
+    sd = TDT[sk]
+    alpha = oz.compute_split_bits(K, sd, oz.select_dot_accum_dtype(sd))
+    a_sl, a_sc = api._split_lines(a, a.stride(1), a.stride(2), M, K, s, alpha, sd, 0)
+    b_sl, b_sc = api._split_lines(b, b.stride(2), b.stride(1), n, K, s, alpha, sd, 0)
+    be = ozd.Backend()
+    want = be.gemm(a_sl, b_sl, a_sc, b_sc, 1, M, n, K, s, torch.float64, False)
+    blocks = -(-n // w)
+    ld = b_sl.shape[-1]
+    g_sl = torch.full((1, blocks, s, w, ld), 77, dtype=torch.int8, device=DEV).view(sd) \
+        if sk != "fp32" else torch.full((1, blocks, s, w, ld), 3.0e30, device=DEV)
+    if sk == "fp16":
+        g_sl = torch.full((1, blocks, s, w, ld), 6.0e4, dtype=sd, device=DEV)
+    g_sc = torch.full((1, blocks, s, w), 1.0e30, device=DEV)
+    for c in range(blocks):
+        c0, c1 = c * w, min(n, (c + 1) * w)
+        g_sl[0, c, :, :c1 - c0] = b_sl[0, :, c0:c1]
+        g_sc[0, c, :, :c1 - c0] = b_sc[0, :, c0:c1]
+    got = be.gemm(a_sl, g_sl, a_sc, g_sc, 1, M, n, K, s, torch.float64, False, b_block_cols=w)
+    assert torch.equal(got, want)
+    assert oz.device_status() == 0
+
+
 @pytest.mark.parametrize("use_ws", [False, True])
 @pytest.mark.parametrize("ik,sk,K", [("fp64", "int8", 8192), ("fp64", "int8", 300),
                                      ("fp32", "fp16", 1000), ("bf16", "int8", 2048),
