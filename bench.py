@@ -207,6 +207,9 @@ def main():
     ap.add_argument("--chunks", type=int, default=0,
                     help="multi-GPU root mode: column blocks B is split and broadcast in "
                          "(0 = auto)")
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "collective"],
+                    help="multi-GPU sharded mode: how B's slices travel (copy-engine pulls "
+                         "from mapped peer buffers, or one NCCL all-gather)")
     ap.add_argument("--dist", default="sharded", choices=["sharded", "root"],
                     help="multi-GPU data layout: A rows x B column panels with an all-gather "
                          "of B's slices (sharded), or B on rank 0 broadcast (root)")

@@ -180,6 +180,27 @@ int oz_cross_gemm_blocked(const void *a_slices, const void *b_slices, const floa
                           uint32_t flags, void *stream);
 
 /*
+ * Peer mappings for the multi-GPU gather (no counterpart in the reference,
+ * which has no multi-GPU path).  One process per GPU: a rank exports the
+ * allocation holding its slice buffer, each peer imports it once and pulls
+ * blocks with oz_copy_async (copy engines over NVLink, no SMs used).
+ */
+#define OZ_IPC_HANDLE_BYTES 64
+
+/* CUDA IPC handle (OZ_IPC_HANDLE_BYTES) of the allocation holding ptr, and
+ * ptr's byte offset inside it. */
+int oz_ipc_export(const void *ptr, void *handle, int64_t *offset);
+
+/* Map a peer's exported allocation into this process: *ptr = base + offset. */
+int oz_ipc_import(const void *handle, int64_t offset, void **ptr);
+
+/* Unmap what oz_ipc_import returned (same ptr and offset). */
+int oz_ipc_close(void *ptr, int64_t offset);
+
+/* Stream-ordered device-to-device copy; either side may be a peer mapping. */
+int oz_copy_async(void *dst, const void *src, int64_t bytes, void *stream);
+
+/*
  * Device-side status: the kernels bound every spin-wait; when a bound is hit
  * they record a code in a device flag and return early (their output is then
  * undefined).  This call synchronises `stream`, returns OZ_OK or

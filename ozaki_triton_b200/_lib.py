@@ -22,6 +22,7 @@ OZ_OK, OZ_ERR_INVALID, OZ_ERR_UNSUPPORTED, OZ_ERR_CUDA, OZ_ERR_TIMEOUT = 0, -1, 
 OZ_RESIDUAL_COMPAT, OZ_RESIDUAL_EXACT = 0, 1
 # oz_cross_gemm flags
 OZ_GEMM_SKIP_TAIL = 1
+OZ_IPC_HANDLE_BYTES = 64
 
 # every function the header declares: name -> (restype, argtypes)
 _i64, _i32, _u32, _vp, _int = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int
@@ -40,6 +41,10 @@ SIGNATURES = {
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_cross_gemm_blocked": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int,
                                      _int, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _u32, _vp]),
+    "oz_ipc_export": (_int, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "oz_ipc_import": (_int, [_vp, _i64, ctypes.POINTER(_vp)]),
+    "oz_ipc_close": (_int, [_vp, _i64]),
+    "oz_copy_async": (_int, [_vp, _vp, _i64, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),
     "oz_last_error": (ctypes.c_char_p, []),
     "oz_version": (ctypes.c_char_p, []),

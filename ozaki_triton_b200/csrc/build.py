@@ -2,7 +2,7 @@
 
     python -m ozaki_triton_b200.csrc.build      # or build() from Python
 
-The three translation units are compiled for sm_100a only (in parallel) and
+The translation units are compiled for sm_100a only (in parallel) and
 linked with the CUDA runtime static, so the .so loads without a CUDA toolkit
 on the library path.  No GPU is needed to build.
 """
@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "liboz_b200.so")
-UNITS = ["oz_api.cu", "oz_split.cu", "oz_gemm.cu"]
+UNITS = ["oz_api.cu", "oz_split.cu", "oz_gemm.cu", "oz_peer.cu"]
 SOURCES = UNITS + ["oz_common.cuh", "oz_log2_table.h"]
 BUILD_DIR = os.path.join(PKG, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -25,8 +25,9 @@ protocol on ``gloo`` ranks.
 
 from __future__ import annotations
 
+import ctypes
 import math
-from typing import Optional, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -222,26 +223,183 @@ def _all_gather_inplace(buf: torch.Tensor, rank: int, group, async_op: bool):
     return dist.all_gather(parts, buf[0, rank].clone(), group=group, async_op=async_op)
 
 
+class PeerBlocks:
+    """Column-blocked slice buffers of this rank, mapped into every peer.
+
+    Two buffer sets alternate between calls, so a rank's split into one set
+    never races a peer still copying from the other; each set is a slice
+    tensor (1, world, s, w, ld) and a scale tensor (1, world, s, w) whose block
+    r is rank r's panel.  The allocations are exported once as CUDA IPC
+    handles, exchanged with ``all_gather_object`` and mapped by every peer;
+    afterwards a block moves with one copy-engine copy over NVLink.
+    """
+
+    def __init__(self, group, shape_sl, shape_sc, slice_dtype, dev):
+        lib = _lib.load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.sl = [torch.empty(shape_sl, dtype=slice_dtype, device=dev) for _ in range(2)]
+        self.sc = [torch.empty(shape_sc, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        mine = []
+        for t in self.sl + self.sc:
+            h = ctypes.create_string_buffer(_lib.OZ_IPC_HANDLE_BYTES)
+            off = ctypes.c_int64()
+            _lib.check(lib.oz_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
+            mine.append((h.raw, off.value))
+        torch.cuda.synchronize(dev)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.peer: Dict[Tuple[int, int], Tuple[int, int]] = {}
+        for q in range(self.world):
+            if q == self.rank:
+                continue
+            for i, (h, off) in enumerate(everyone[q]):
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.oz_ipc_import(h, off, ctypes.byref(ptr)))
+                self.peer[(q, i)] = (ptr.value, off)
+        self.dev = dev
+        self.copy_streams = []
+        self.gemm_streams = []
+        self.calls = 0
+
+    def streams(self, copies: int, gemms: int):
+        while len(self.copy_streams) < copies:
+            self.copy_streams.append(torch.cuda.Stream(self.dev))
+        while len(self.gemm_streams) < gemms:
+            self.gemm_streams.append(torch.cuda.Stream(self.dev))
+        return self.copy_streams[:copies], self.gemm_streams[:gemms]
+
+    def close(self):
+        lib = _lib.load()
+        for ptr, off in self.peer.values():
+            lib.oz_ipc_close(ptr, off)
+        self.peer = {}
+
+
+_PEER_CACHE: Dict[tuple, PeerBlocks] = {}
+
+# streams of the p2p transport: copies in flight at once (blocks arrive one
+# after another, so the first block GEMMs start early) and streams the block
+# GEMMs run on (None = one per peer block: every arrived block may start)
+P2P_COPY_STREAMS = 2
+P2P_GEMM_STREAMS: Optional[int] = None
+
+
+def release_peer_buffers(group=None) -> None:
+    """Unmap and free the cached peer buffers (collective: every rank calls it)."""
+    for key in [k for k in _PEER_CACHE if k[0] == id(group)]:
+        pb = _PEER_CACHE.pop(key)
+        torch.cuda.synchronize(pb.sl[0].device)
+        dist.barrier(group=group)          # no peer copies from our buffers any more
+        pb.close()
+        dist.barrier(group=group)          # every peer has unmapped them
+
+
+def _peer_blocks(group, shape_sl, shape_sc, slice_dtype, dev) -> PeerBlocks:
+    key = (id(group), tuple(shape_sl), slice_dtype, str(dev))
+    pb = _PEER_CACHE.get(key)
+    if pb is None:
+        pb = _PEER_CACHE[key] = PeerBlocks(group, shape_sl, shape_sc, slice_dtype, dev)
+    return pb
+
+
+def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode, n, w, ld,
+                 skip_tail, group):
+    """Pipelined gather: every block GEMM starts as soon as its block is here."""
+    dev = A_local.device
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    m_loc, k = A_local.shape
+    pb = _peer_blocks(group, (1, world, num_splits, w, ld), (1, world, num_splits, w),
+                      slice_dtype, dev)
+    par = pb.calls % 2
+    pb.calls += 1
+    sl, sc = pb.sl[par], pb.sc[par]
+    cur = torch.cuda.current_stream(dev)
+    _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, sl[0, rank],
+                 sc[0, rank])
+    # every rank's panel is split, and no peer still copies from the buffer
+    # set this call reuses (its copies of two calls ago ended before it
+    # entered this all-reduce)
+    dist.all_reduce(pb.flag, group=group)
+    ready = torch.cuda.Event()
+    ready.record(cur)
+    A3 = A_local.reshape(1, m_loc, k)
+    a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
+                               slice_dtype, mode)
+    a_ready = torch.cuda.Event()
+    a_ready.record(cur)
+    blocks = -(-n // w)
+    order = [(rank + d) % world for d in range(1, world)]
+    order = [j for j in order if j < blocks]
+    copy_streams, gemm_streams = pb.streams(
+        max(1, P2P_COPY_STREAMS), max(1, P2P_GEMM_STREAMS or len(order)))
+    lib = _lib.load()
+    blk_sl = sl[0, 0].numel() * sl.element_size()
+    blk_sc = sc[0, 0].numel() * 4
+    arrived = {}
+    for i, j in enumerate(order):
+        cs = copy_streams[i % len(copy_streams)]
+        cs.wait_event(ready)
+        src_sl = pb.peer[(j, par)][0] + j * blk_sl
+        src_sc = pb.peer[(j, 2 + par)][0] + j * blk_sc
+        _lib.check(lib.oz_copy_async(sl[0, j].data_ptr(), src_sl, blk_sl, cs.cuda_stream))
+        _lib.check(lib.oz_copy_async(sc[0, j].data_ptr(), src_sc, blk_sc, cs.cuda_stream))
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        arrived[j] = ev
+    c = torch.empty((1, m_loc, n), dtype=A_local.dtype, device=dev)
+
+    def block_gemm(j):
+        c0, c1 = j * w, min(n, (j + 1) * w)
+        backend.gemm(a_sl, sl[:, j:j + 1], a_sc, sc[:, j:j + 1], 1, m_loc, c1 - c0, k,
+                     num_splits, A_local.dtype, skip_tail, out=c, col0=c0, b_block_cols=w)
+
+    if rank < blocks:
+        block_gemm(rank)
+    for i, j in enumerate(order):
+        gs = gemm_streams[i % len(gemm_streams)]
+        gs.wait_event(a_ready)
+        gs.wait_event(arrived[j])
+        with torch.cuda.stream(gs):
+            block_gemm(j)
+    for gs in gemm_streams:
+        cur.wait_stream(gs)
+        for t in (c, a_sl, a_sc):
+            t.record_stream(gs)
+    return c
+
+
 def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_splits: int = 3,
                          slice_dtype: torch.dtype = torch.float16, *, n: Optional[int] = None,
                          group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
+                         transport: str = "collective",
                          backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B with A sharded by rows and B by column panels.
 
     Rank r passes its rows of A (M_local, K) (any split of the rows) and its
     panel of B's columns (K, N_r), the columns ``column_panel(N, world, r)``;
     ``n`` (N) may be given to save one small collective.  Each rank splits
-    only its own panel and its own rows; one all-gather then moves the int8
-    (or float) slices of every panel to every rank -- for int8 slices half the
-    bytes of the fp64 panels -- into a column-blocked buffer that the GEMM
-    reads in place.  The split of A's rows overlaps the all-gather.  Returns
-    this rank's rows of C (M_local, N), bit-identical to the same rows of the
-    single-GPU ``ozaki_matmul``.
+    only its own panel and its own rows; the int8 (or float) slices of every
+    panel -- for int8 slices half the bytes of the fp64 panels -- then reach
+    every rank in a column-blocked buffer that the GEMM reads in place.
+    Returns this rank's rows of C (M_local, N), bit-identical to the same rows
+    of the single-GPU ``ozaki_matmul``.
+
+    ``transport``:
+    * ``"collective"``: one all-gather (NCCL, or gloo on CPU) while the A rows
+      are split, then one GEMM over all of N;
+    * ``"p2p"`` (NCCL groups of one process per GPU): every rank maps its
+      peers' slice buffers once (CUDA IPC) and pulls block after block with
+      copy-engine copies; the GEMM of each block starts as soon as it has
+      arrived, on a stream of its own, so the transfer overlaps the GEMMs.
     """
     backend = backend or Backend()
     dev = A_local.device
     _check_args(A_local.dtype, num_splits, slice_dtype)
     assert A_local.dtype == B_local.dtype
+    assert transport in ("collective", "p2p"), f"unknown transport {transport!r}"
     m_loc, k = A_local.shape
     assert B_local.shape[0] == k, f"contraction dim mismatch: {A_local.shape} @ {B_local.shape}"
     rank = dist.get_rank(group)
@@ -260,6 +418,10 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
     w = block_width(n, world)
     if world == 1 or n == 0:
         w = max(n, 1)
+    if transport == "p2p" and world > 1 and n > 0:
+        c = _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode, n, w,
+                         ld, skip_tail, group)
+        return c.reshape(m_loc, n)
     # one block per rank (blocks past ceil(n / w) stay empty and are not read)
     b_sl, b_sc = _blocked_buffers(world, num_splits, w, ld, slice_dtype, dev)
     _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, b_sl[0, rank],

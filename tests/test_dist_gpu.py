@@ -49,9 +49,14 @@ def _worker(rank, world, port, out_dir):
         for n in (300, 1000):
             Bn = (torch.rand(700, n, generator=g, dtype=torch.float64) - 0.5) * 3.0
             p0, p1 = ozd.column_panel(n, world, rank)
-            cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4, torch.int8)
-            ok1 = ok1 and torch.equal(cs, oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4,
-                                                           torch.int8)[lo:hi])
+            want_n = oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4, torch.int8)[lo:hi]
+            # collective all-gather, then copy-engine pulls (three calls: both
+            # buffer sets of the alternation, and the reuse of the first)
+            for transport in ("collective", "p2p", "p2p", "p2p"):
+                cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4,
+                                              torch.int8, transport=transport)
+                ok1 = ok1 and torch.equal(cs, want_n)
+        ozd.release_peer_buffers()
         A4 = torch.randn(4, 1, 64, 96, generator=g, dtype=torch.float64)
         B4 = torch.randn(1, 3, 96, 40, generator=g, dtype=torch.float64)
         cb, s0, s1 = ozd.ozaki_matmul_batches(A4.to(dev), B4.to(dev), 3, torch.float16)

@@ -116,6 +116,31 @@ def test_argument_validation_without_launch():
     assert gemm(m=0) == _lib.OZ_OK
 
 
+def test_blocked_gemm_and_peer_entries_validate_without_a_gpu():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)      # never dereferenced: validation fails first
+    # B column block width: 0, >= n or a multiple of 128
+    rc = lib.oz_cross_gemm_blocked(p, p, p, p, 1, 256, 1000, 64, 128, 2, _lib.OZ_I8, _lib.OZ_F64,
+                                   None, None, 1, 1, 200, p, 1000, 0, None)
+    assert rc == _lib.OZ_ERR_INVALID and "block width" in lib.oz_last_error().decode()
+    rc = lib.oz_cross_gemm_blocked(p, p, p, p, 1, 256, 1000, 64, 128, 2, _lib.OZ_I8, _lib.OZ_F64,
+                                   None, None, 1, 1, -128, p, 1000, 0, None)
+    assert rc == _lib.OZ_ERR_INVALID
+    # empty problems return before any device work, whatever the block width
+    assert lib.oz_cross_gemm_blocked(p, p, p, p, 1, 0, 1000, 64, 128, 2, _lib.OZ_I8, _lib.OZ_F64,
+                                     None, None, 1, 1, 256, p, 1000, 0, None) == _lib.OZ_OK
+    # peer mappings and copies
+    off = ctypes.c_int64()
+    h = ctypes.create_string_buffer(_lib.OZ_IPC_HANDLE_BYTES)
+    assert lib.oz_ipc_export(None, h, ctypes.byref(off)) == _lib.OZ_ERR_INVALID
+    assert lib.oz_ipc_import(None, 0, None) == _lib.OZ_ERR_INVALID
+    assert lib.oz_ipc_import(h, -1, ctypes.byref(ctypes.c_void_p())) == _lib.OZ_ERR_INVALID
+    assert lib.oz_ipc_close(None, 0) == _lib.OZ_ERR_INVALID
+    assert lib.oz_copy_async(p, p, -1, None) == _lib.OZ_ERR_INVALID
+    assert lib.oz_copy_async(None, p, 16, None) == _lib.OZ_ERR_INVALID
+    assert lib.oz_copy_async(p, p, 0, None) == _lib.OZ_OK
+
+
 def test_policy_tables_match_reference():
     # ozaki_triton.py:36-41, 62-73
     assert oz.SLICE_DTYPE_INFO[torch.float32] == (23, False)
