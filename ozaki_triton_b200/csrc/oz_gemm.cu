@@ -10,11 +10,13 @@
 // to the reference.
 //
 // Structure (one persistent CTA per SM, 10 warps):
-//   warp 0     TMA producer: 128x128-byte K-major tiles (128-byte swizzle) of
-//              A_i and B_j into two shared-memory rings (A ring, B ring).
+//   warp 0     TMA producer: per 128-byte K block, the A_i tile and the
+//              stacked tiles of all B_j (one 3-D box) into one ring stage.
 //   warp 1     TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2-9  epilogue: tcgen05.ld of the int32/fp32 accumulators, scaling,
-//              fp64/fp32 outer accumulation in registers, store of C.
+//   warps 2-9  epilogue: the tile's B scales staged once in shared memory,
+//              tcgen05.ld of the int32/fp32 accumulators 32 columns per wait,
+//              scaling, fp64/fp32 outer accumulation in registers (200
+//              registers per thread, no spills), store of C.
 // Per output tile (128 rows x NT columns) the kernel runs one "pass" per A
 // slice i: a full K loop that accumulates the pair products A_i B_j for every
 // j into s TMEM accumulators of NT columns each (s * NT <= 512 columns).  A_i
@@ -70,6 +72,9 @@ __host__ __device__ inline int stage_bytes(int s, int nt, int pair) {
   return a_tile_bytes() + s * (nt / pair) * kKBytes;
 }
 
+// B scales of a tile staged for the epilogue: two tiles x s slices x NT floats.
+__host__ __device__ inline int scale_stage_bytes(int s, int nt) { return 2 * s * nt * 4; }
+
 template <int OUTK> struct OutT;
 template <> struct OutT<OZ_F64> { using acc = double; using store = double; };
 template <> struct OutT<OZ_F32> { using acc = float; using store = float; };
@@ -122,8 +127,10 @@ __device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, 
 // Rg columns of a group come from the leader's B rows (tile columns
 // [0, NT/2)), the next Rg from the peer's (tile columns [NT/2, NT)), with
 // Rg = NT/2 * (slices in the group).
+// 200 registers x 320 threads fit the register file at one CTA per SM; the
+// epilogue's 64 fp64 accumulators per thread need them (no spills).
 template <int KIND, int OUTK, int NT, int PAIR>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __maxnreg__(200)
     cross_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
   using ACC = typename OutT<OUTK>::acc;
@@ -146,7 +153,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *acc_full = empty + kMaxStages;  // [2]
   uint64_t *acc_empty = acc_full + 2;     // [2]
   uint64_t *drain = acc_empty + 2;        // [1]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *sb_ready = drain + 1;         // [2] B scales of a tile staged
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sb_ready + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -166,6 +174,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[i], PAIR * kEpiWarps * 32);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&sb_ready[i], kEpiWarps * 32);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_a);
@@ -298,16 +307,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int e = warp - 2;
     const int sub = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = e >> 2;                  // which half of the NT tile columns
+    const int et = threadIdx.x - 64;          // epilogue thread 0..255
     const int row = (int)rank * kBM + sub * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(sub * 32) << 16);
     const uint32_t empty_addr0 = leader_addr(&acc_empty[0]);
     const uint32_t empty_addr1 = leader_addr(&acc_empty[1]);
+    // B scales of the current tile, [2 tiles][s][NT], read as warp-wide broadcasts
+    float *sb_stage = reinterpret_cast<float *>(smem + S * sbytes + kBarrierBytes);
     ACC out[NH];
 #pragma unroll
     for (int x = 0; x < NH; ++x) out[x] = (ACC)0;
     uint32_t pass = 0;
+    int tile_iter = 0;
     bool ok = true;
-    for (int t = unit; ok && t < p.num_tiles; t += units) {
+    for (int t = unit; ok && t < p.num_tiles; t += units, ++tile_iter) {
       int b, mb, nb;
       tile_coords(p, t, b, mb, nb);
       const int ai = p.a_index ? p.a_index[b] : b;
@@ -315,20 +328,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m = mb * TM + row;
       const int n0 = nb * NT + half * NH;
       const int blk = (nb * NT) / p.bw;
+      // stage the tile's B scales; a warp passes the staging barrier of tile
+      // t + 1 only when every epilogue warp has finished tile t, so the
+      // buffer of tile t + 2 is free when it is written
+      float *sbt = sb_stage + (tile_iter & 1) * s * NT;
+      {
+        const float *src = p.b_scales + ((int64_t)bi * p.bblocks + blk) * s * p.bw;
+        const int c0 = nb * NT - blk * p.bw;   // first tile column inside its block
+        for (int q = et; q < s * NT; q += kEpiWarps * 32) {
+          const int j = q / NT, x = q - j * NT;
+          sbt[q] = (nb * NT + x < p.n) ? __ldg(src + (int64_t)j * p.bw + c0 + x) : 0.f;
+        }
+      }
+      mbar_arrive(&sb_ready[tile_iter & 1]);
+      ok = mbar_wait_bounded(&sb_ready[tile_iter & 1], (tile_iter >> 1) & 1, abort_flag,
+                             DEV_TIMEOUT_EPILOGUE);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       for (int i = 0; i < s; ++i, ++pass) {
         const int js = p.skip_tail ? s - i : s;
         const int buf = pass % nbuf;
         const uint32_t use = pass / nbuf;
+        const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         // every lane waits, then the warp agrees (tcgen05.ld needs a converged warp)
         ok = mbar_wait_bounded(&acc_full[buf], use & 1, abort_flag, DEV_TIMEOUT_EPILOGUE);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         for (int j = 0; j < js; ++j) {
-          // scales of B slice j in this tile's column block, indexed by global column
-          const float *sbp = p.b_scales + (((int64_t)bi * p.bblocks + blk) * s + j) * p.bw -
-                             (int64_t)blk * p.bw;
+          const float *sbj = sbt + j * NT + half * NH;
           const int g = j / SPG, jj = j % SPG;
           int col;
           if constexpr (PAIR == 2) {
@@ -338,19 +366,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             col = buf * s * NT + g * 256 + jj * NT + half * NH;
           }
 #pragma unroll
-          for (int c = 0; c < NH / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld16(lane_addr + (uint32_t)(col + c * 16), r);
-            tmem_ld_wait();
+          for (int c = 0; c < NH / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 32), r);
+            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 32 + 16), r + 16);
+            tmem_ld_wait32(r);
 #pragma unroll
-            for (int x = 0; x < 16; ++x) {
-              const int cc = n0 + c * 16 + x;
-              const float sb = (cc < p.n) ? __ldg(sbp + cc) : 0.f;
+            for (int x = 0; x < 32; ++x) {
+              const float sb = sbj[c * 32 + x];
               float v;
               if constexpr (KIND == 0) v = __int2float_rn((int)r[x]);
               else v = __uint_as_float(r[x]);
               v = __fmul_rn(__fmul_rn(v, sa), sb);
-              out[c * 16 + x] = acc_add<ACC>(out[c * 16 + x], v);
+              out[c * 32 + x] = acc_add<ACC>(out[c * 32 + x], v);
             }
           }
         }
@@ -453,7 +481,8 @@ template <int KIND, int OUTK, int NT, int PAIR>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
                 cudaStream_t st) {
   auto kern = cross_gemm_kernel<KIND, OUTK, NT, PAIR>;
-  const int smem = p.stages * stage_bytes(p.s, NT, PAIR) + 1024 + kBarrierBytes;
+  const int smem = p.stages * stage_bytes(p.s, NT, PAIR) + 1024 + kBarrierBytes +
+                   scale_stage_bytes(p.s, NT);
   if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                smem),
                           "cudaFuncSetAttribute(cross_gemm)"))
@@ -611,7 +640,8 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
   p.idesc = make_idesc(slice_dtype, kBM * pair);
-  p.stages = min(kMaxStages, kSmemBudget / stage_bytes(num_splits, nt, pair));
+  p.stages = min(kMaxStages, (kSmemBudget - scale_stage_bytes(num_splits, nt)) /
+                                 stage_bytes(num_splits, nt, pair));
 
   const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
   if (pair == 2) {
