@@ -14,9 +14,8 @@
 //              stacked tiles of all B_j (one 3-D box) into one ring stage.
 //   warp 1     TMEM allocator + single-thread tcgen05.mma issuer.
 //   warps 2-9  epilogue: the tile's B scales staged once in shared memory,
-//              tcgen05.ld of the int32/fp32 accumulators 32 columns per wait,
-//              scaling, fp64/fp32 outer accumulation in registers (200
-//              registers per thread, no spills), store of C.
+//              tcgen05.ld of the int32/fp32 accumulators, scaling, fp64/fp32
+//              outer accumulation in registers, store of C.
 // Per output tile (128 rows x NT columns) the kernel runs one "pass" per A
 // slice i: a full K loop that accumulates the pair products A_i B_j for every
 // j into s TMEM accumulators of NT columns each (s * NT <= 512 columns).  A_i
@@ -127,10 +126,11 @@ __device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, 
 // Rg columns of a group come from the leader's B rows (tile columns
 // [0, NT/2)), the next Rg from the peer's (tile columns [NT/2, NT)), with
 // Rg = NT/2 * (slices in the group).
-// 200 registers x 320 threads fit the register file at one CTA per SM; the
-// epilogue's 64 fp64 accumulators per thread need them (no spills).
+// 320 threads: registers are split per SM sub-partition (16K each, up to 3
+// warps on one), so a thread gets at most 168 -- 128 of them hold the
+// epilogue's 64 fp64 accumulators.
 template <int KIND, int OUTK, int NT, int PAIR>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     cross_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
   using ACC = typename OutT<OUTK>::acc;
@@ -366,19 +366,18 @@ __global__ void __maxnreg__(200)
             col = buf * s * NT + g * 256 + jj * NT + half * NH;
           }
 #pragma unroll
-          for (int c = 0; c < NH / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 32), r);
-            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 32 + 16), r + 16);
-            tmem_ld_wait32(r);
+          for (int c = 0; c < NH / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 16), r);
+            tmem_ld_wait16(r);
 #pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              const float sb = sbj[c * 32 + x];
+            for (int x = 0; x < 16; ++x) {
+              const float sb = sbj[c * 16 + x];
               float v;
               if constexpr (KIND == 0) v = __int2float_rn((int)r[x]);
               else v = __uint_as_float(r[x]);
               v = __fmul_rn(__fmul_rn(v, sa), sb);
-              out[c * 32 + x] = acc_add<ACC>(out[c * 32 + x], v);
+              out[c * 16 + x] = acc_add<ACC>(out[c * 16 + x], v);
             }
           }
         }
