@@ -51,6 +51,18 @@ template <> struct SliceT<OZ_F16> { using type = __half; };
 template <> struct SliceT<OZ_BF16> { using type = __nv_bfloat16; };
 template <> struct SliceT<OZ_F32> { using type = float; };
 
+// What a quantisation step hands to the store: the slice value itself, or
+// for int8 slices a 32-bit word whose low byte is the int8 value (a
+// magic-number float's bits or the clamped integer), so that four of them
+// pack into one word with byte permutes.
+template <int SK> struct QOut { using type = typename SliceT<SK>::type; };
+template <> struct QOut<OZ_I8> { using type = uint32_t; };
+template <int SK>
+__device__ __forceinline__ typename SliceT<SK>::type to_slice(typename QOut<SK>::type q) {
+  if constexpr (SK == OZ_I8) return (int8_t)(q & 0xFFu);
+  else return q;
+}
+
 template <typename RD> struct Level {
   float scale;   // stored scale (fp32 power of two)
   RD scale_rd;   // the same value in rd
@@ -173,23 +185,16 @@ __device__ __forceinline__ int ceil_log2_table(float m) {
 
 struct LevelP {
   float scale;      // stored scale 2^e
-  double inv_d;     // 2^-e
-  float inv1, inv2; // 2^-e == inv1 * inv2, both exact floats
-  bool big;         // 2^-e is not a float: two multiplies
+  int e;
   __device__ __forceinline__ void init(float row_max, int alpha) {
     const float m = fmaxf(1e-38f, row_max);
-    const int e = ceil_log2_table(m) - alpha;     // e in [-149, 127]
+    e = ceil_log2_table(m) - alpha;               // e in [-149, 127]
     scale = pow2f(e);
-    inv_d = pow2d(-e);
-    big = -e > 127;
-    if (big) {
-      inv1 = 18446744073709551616.0f;             // 2^64
-      inv2 = pow2f(-e - 64);
-    } else {
-      inv1 = 1.0f;
-      inv2 = pow2f(-e);
-    }
   }
+  __device__ __forceinline__ double inv_d() const { return pow2d(-e); }   // 2^-e
+  // 2^-e is not a float when -e > 127: then it is 2^64 * 2^(-e-64)
+  __device__ __forceinline__ bool big() const { return -e > 127; }
+  __device__ __forceinline__ float inv2() const { return pow2f(big() ? -e - 64 : -e); }
 };
 
 constexpr float kMagicF = 12582912.0f;            // 1.5 * 2^23
@@ -203,7 +208,11 @@ __device__ __forceinline__ float small_int_to_float(int n) {
 __device__ __forceinline__ double int_to_double_exact(int n) {
   return __dsub_rn(__hiloint2double(0x43380000 + (n >> 31), n), 6755399441055744.0);
 }
-__device__ __forceinline__ int clamp_i8(int n) { return max(-128, min(127, n)); }
+// |x| < 128.5 for every level (the scale is at least the line maximum / 2^7,
+// up to float32 rounding of the maximum and of its log2), so rounding half
+// away from zero gives at least -128 and at most +128: only +128 needs the
+// reference's clamp to 127.
+__device__ __forceinline__ int clamp_i8(int n) { return min(127, n); }
 
 template <int SK> __device__ __forceinline__ typename SliceT<SK>::type slice_from_f64(double x) {
   if constexpr (SK == OZ_F16) {
@@ -232,15 +241,15 @@ template <int SK> __device__ __forceinline__ float slice_to_f32(typename SliceT<
 // level on an fp64 residual; the next residual goes to rn_d (EXACT) or,
 // rounded to fp32 like the reference's residual buffer, to rn_f
 template <int SK, bool EXACT>
-__device__ __forceinline__ typename SliceT<SK>::type step_f64(double r, const LevelP &lv, bool upd,
-                                                              double &rn_d, float &rn_f) {
-  const double x = __dmul_rn(r, lv.inv_d);
+__device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv_d, float scale,
+                                                            bool upd, double &rn_d, float &rn_f) {
+  const double x = __dmul_rn(r, inv_d);
   double qd;
-  typename SliceT<SK>::type q;
+  typename QOut<SK>::type q;
   if constexpr (SK == OZ_I8) {
     const double t = __dadd_rn(x, copysign(0.5, x));
     const int n = clamp_i8(__double2int_rz(t));
-    q = (int8_t)n;
+    q = (uint32_t)n;
     qd = int_to_double_exact(n);
   } else {
     q = slice_from_f64<SK>(x);
@@ -248,7 +257,7 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f64(double r, const Le
   }
   if (upd) {
     // q * scale is exact, so one fused rounding equals the reference's r - q*s
-    const double d = __fma_rn(-qd, (double)lv.scale, r);
+    const double d = __fma_rn(-qd, (double)scale, r);
     if constexpr (EXACT) rn_d = d;
     else rn_f = __double2float_rn(d);
   }
@@ -268,18 +277,19 @@ __device__ __forceinline__ float round_q(float x) {
   const float a = fabsf(x);
   const float t = EXACT_HALF ? __fadd_rz(a, 0.5f) : __fadd_rn(a, 0.5f);
   const float qa = __fsub_rn(__fadd_rz(t, kMagicF), kMagicF);   // floor(t), exact
-  return fmaxf(fminf(copysignf(qa, x), 127.0f), -128.0f);
+  return fminf(copysignf(qa, x), 127.0f);     // floor(t) <= 128: see clamp_i8
 }
-// the int8 bit pattern of an integer-valued float q in [-128, 127]
-__device__ __forceinline__ int8_t q_byte(float q) {
-  return (int8_t)(__float_as_uint(__fadd_rn(q, kMagicF)) & 0xFFu);
+// a word whose low byte is the int8 bit pattern of an integer-valued float q
+// in [-128, 127]: 1.5 * 2^23 + q has q's two's complement in its low bits
+__device__ __forceinline__ uint32_t q_word(float q) {
+  return __float_as_uint(__fadd_rn(q, kMagicF));
 }
 
 // x = r * 2^-e in fp32: one multiply, or two when 2^-e exceeds the float range
 template <bool BIG>
-__device__ __forceinline__ float scale_down(float r, const LevelP &lv) {
-  if constexpr (BIG) return __fmul_rn(__fmul_rn(r, lv.inv1), lv.inv2);
-  else return __fmul_rn(r, lv.inv2);
+__device__ __forceinline__ float scale_down(float r, float inv2) {
+  if constexpr (BIG) return __fmul_rn(__fmul_rn(r, 18446744073709551616.0f), inv2);   // 2^64
+  else return __fmul_rn(r, inv2);
 }
 
 // level >= 1 of an fp64 input (fp32-valued residual, fp64 reference
@@ -287,16 +297,16 @@ __device__ __forceinline__ float scale_down(float r, const LevelP &lv) {
 // exact rounding half away from zero (x + 0.5 needs at most 33 bits whenever
 // the result can be nonzero)
 template <int SK, bool BIG>
-__device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, const LevelP &lv,
-                                                                    bool upd) {
-  const float x = scale_down<BIG>(r, lv);
+__device__ __forceinline__ typename QOut<SK>::type step_f32_exact(float &r, float inv2,
+                                                                  float scale, bool upd) {
+  const float x = scale_down<BIG>(r, inv2);
   if constexpr (SK == OZ_I8) {
     const float q = round_q<true>(x);
-    if (upd) r = __fmaf_rn(-q, lv.scale, r);   // exact
-    return q_byte(q);
+    if (upd) r = __fmaf_rn(-q, scale, r);   // exact
+    return q_word(q);
   } else {
     const auto q = slice_from_f32<SK>(x);
-    if (upd) r = __fmaf_rn(-slice_to_f32<SK>(q), lv.scale, r);
+    if (upd) r = __fmaf_rn(-slice_to_f32<SK>(q), scale, r);
     return q;
   }
 }
@@ -304,16 +314,16 @@ __device__ __forceinline__ typename SliceT<SK>::type step_f32_exact(float &r, co
 // every level of a non-fp64 input (fp32 residual, fp32 reference arithmetic):
 // trunc(fl32(x +- 0.5)) = sign(x) * floor(fl32(|x| + 0.5))
 template <int SK, bool BIG>
-__device__ __forceinline__ typename SliceT<SK>::type step_f32_rd(float &r, const LevelP &lv,
-                                                                 bool upd) {
-  const float x = scale_down<BIG>(r, lv);   // == r / scale, rounded once
+__device__ __forceinline__ typename QOut<SK>::type step_f32_rd(float &r, float inv2, float scale,
+                                                               bool upd) {
+  const float x = scale_down<BIG>(r, inv2);   // == r / scale, rounded once
   if constexpr (SK == OZ_I8) {
     const float q = round_q<false>(x);
-    if (upd) r = __fsub_rn(r, __fmul_rn(q, lv.scale));
-    return q_byte(q);
+    if (upd) r = __fsub_rn(r, __fmul_rn(q, scale));
+    return q_word(q);
   } else {
     const auto q = slice_from_f32<SK>(x);
-    if (upd) r = __fsub_rn(r, __fmul_rn(slice_to_f32<SK>(q), lv.scale));
+    if (upd) r = __fsub_rn(r, __fmul_rn(slice_to_f32<SK>(q), scale));
     return q;
   }
 }
@@ -338,6 +348,7 @@ __device__ __forceinline__ void tma_load_3d_plain(void *dst, const CUtensorMap *
 // threads of the line.
 template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
   using ST = typename SliceT<SK>::type;
+  using QT = typename QOut<SK>::type;
   static constexpr bool F64IN = sizeof(TIn) == 8;
   double vd[F64IN ? NV : 1];
   float vf[NV];
@@ -347,9 +358,9 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
     else vf[i] = InTraits<TIn>::to_float(v);
   }
 
-  // emit(l, i, q) stores one slice element and must not synchronise (it runs
-  // inside data-dependent branches); end_level(l) runs once per level on
-  // every thread, after all of that level's emits.
+  // emit(l, i, q) stores one slice element (q as QOut: see there) and must
+  // not synchronise (it runs inside data-dependent branches); end_level(l)
+  // runs once per level on every thread, after all of that level's emits.
   template <typename Reduce, typename Emit, typename Scale, typename EndLevel>
   __device__ __forceinline__ void run(int s, int alpha, Reduce reduce, Emit emit, Scale put_scale,
                                       EndLevel end_level) {
@@ -373,30 +384,33 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
       put_scale(l, lv.scale);
       if (on_f64) {
         if constexpr (F64IN) {
+          const double inv_d = lv.inv_d();
 #pragma unroll
           for (int i = 0; i < NV; ++i) {
             double nd = 0.0;
             float nf = 0.f;
-            ST q = step_f64<SK, EXACT>(vd[i], lv, upd, nd, nf);
+            QT q = step_f64<SK, EXACT>(vd[i], inv_d, lv.scale, upd, nd, nf);
             if constexpr (EXACT) vd[i] = nd;
             else vf[i] = nf;
             emit(l, i, q);
           }
         }
-      } else if (!lv.big) {
+      } else if (!lv.big()) {
+        const float inv2 = lv.inv2();
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-          ST q;
-          if constexpr (F64IN) q = step_f32_exact<SK, false>(vf[i], lv, upd);
-          else q = step_f32_rd<SK, false>(vf[i], lv, upd);
+          QT q;
+          if constexpr (F64IN) q = step_f32_exact<SK, false>(vf[i], inv2, lv.scale, upd);
+          else q = step_f32_rd<SK, false>(vf[i], inv2, lv.scale, upd);
           emit(l, i, q);
         }
       } else {
+        const float inv2 = lv.inv2();
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-          ST q;
-          if constexpr (F64IN) q = step_f32_exact<SK, true>(vf[i], lv, upd);
-          else q = step_f32_rd<SK, true>(vf[i], lv, upd);
+          QT q;
+          if constexpr (F64IN) q = step_f32_exact<SK, true>(vf[i], inv2, lv.scale, upd);
+          else q = step_f32_rd<SK, true>(vf[i], inv2, lv.scale, upd);
           emit(l, i, q);
         }
       }
@@ -412,12 +426,42 @@ constexpr int kRowCTA = 512;
 constexpr int kRowMaxStages = 4;
 constexpr int kRowSmem = 200 * 1024;
 
+// Elements per thread and chunk of the row kernel: 16-byte chunks of the
+// input, except fp64, whose 32-byte chunks (two 16-byte reads) give int8
+// slices 4-byte stores.
+template <typename TIn> __host__ __device__ constexpr int row_vec() {
+  return sizeof(TIn) == 8 ? 4 : 16 / (int)sizeof(TIn);
+}
+
+// VEC slice values -> one store.  int8: the low bytes of VEC QOut words,
+// packed with byte permutes (3 per 4 values).
+template <int SK, int VEC>
+__device__ __forceinline__ void store_slices(typename SliceT<SK>::type *dst,
+                                             const typename QOut<SK>::type (&q)[VEC]) {
+  if constexpr (SK == OZ_I8) {
+    static_assert(VEC % 4 == 0, "int8 slices are stored 4 at a time");
+    uint32_t w[VEC / 4];
+#pragma unroll
+    for (int j = 0; j < VEC / 4; ++j)
+      w[j] = __byte_perm(__byte_perm(q[4 * j], q[4 * j + 1], 0x0040),
+                         __byte_perm(q[4 * j + 2], q[4 * j + 3], 0x0040), 0x5410);
+    if constexpr (VEC == 4) *reinterpret_cast<uint32_t *>(dst) = w[0];
+    else *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+  } else {
+    Pack<typename SliceT<SK>::type, VEC> pq;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) pq.e[j] = q[j];
+    *reinterpret_cast<Pack<typename SliceT<SK>::type, VEC> *>(dst) = pq;
+  }
+}
+
 // Persistent kernel: each iteration takes RPS = 512 / T whole rows; a group
 // of T threads owns a row.  Rows arrive by bulk TMA copies into a ring of NS
 // stages, are moved to registers, and the stage is refilled with a later
 // iteration's rows while the levels are computed.  Thread `tl` of a row
-// holds elements [(c*T + tl)*VEC, +VEC) for c < NCH (16-byte chunks: the
-// shared-memory reads are conflict-free and the slice stores coalesce).
+// holds elements [(c*T + tl)*VEC, +VEC) for c < NCH (16- or 32-byte chunks:
+// the shared-memory reads are conflict-free or 2-way, the slice stores
+// coalesce).
 template <typename TIn, int SK, int T, int NCH, bool EXACT>
 __global__ void __launch_bounds__(kRowCTA, 1)
     split_rows_tma(const TIn *__restrict__ in, int64_t stride_b, int64_t stride_line, int lines,
@@ -425,7 +469,8 @@ __global__ void __launch_bounds__(kRowCTA, 1)
                    typename SliceT<SK>::type *__restrict__ out, float *__restrict__ scales, int NS,
                    int rowp) {
   using ST = typename SliceT<SK>::type;
-  constexpr int VEC = 16 / (int)sizeof(TIn);
+  using QT = typename QOut<SK>::type;
+  constexpr int VEC = row_vec<TIn>();
   constexpr int NV = NCH * VEC;
   constexpr int RPS = kRowCTA / T;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -455,14 +500,16 @@ __global__ void __launch_bounds__(kRowCTA, 1)
     for (int i = 0; i < NS && blockIdx.x + (int64_t)i * gridDim.x < groups; ++i)
       issue(blockIdx.x + (int64_t)i * gridDim.x, i);
 
-  // which of this thread's chunks lie inside the row pitch (written), and
-  // inside K (read); fixed for the whole kernel
-  uint32_t in_ld = 0, in_k = 0;
+  // which of this thread's chunks lie inside the row pitch (written), wholly
+  // inside K (read as a vector), or straddle K (read element by element);
+  // fixed for the whole kernel
+  uint32_t in_ld = 0, in_k = 0, part_k = 0;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int k0 = (c * T + tl) * VEC;
     in_ld |= (uint32_t)(k0 < ld) << c;
-    in_k |= (uint32_t)(k0 < K) << c;
+    in_k |= (uint32_t)(k0 + VEC <= K) << c;
+    part_k |= (uint32_t)(k0 < K && k0 + VEC > K) << c;
   }
 
   volatile int abort_flag = 0;
@@ -479,10 +526,14 @@ __global__ void __launch_bounds__(kRowCTA, 1)
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       Pack<TIn, VEC> pk;
-      if (active && ((in_k >> c) & 1)) pk = *reinterpret_cast<const Pack<TIn, VEC> *>(srow + c * T * VEC);
-      else {
+      if (active && ((in_k >> c) & 1)) {
+        pk = *reinterpret_cast<const Pack<TIn, VEC> *>(srow + c * T * VEC);
+      } else {
+        const int k0 = (c * T + tl) * VEC;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) pk.e[e] = (TIn)0.0f;
+        for (int e = 0; e < VEC; ++e)
+          pk.e[e] = (active && ((part_k >> c) & 1) && k0 + e < K) ? srow[c * T * VEC + e]
+                                                                  : (TIn)0.0f;
       }
 #pragma unroll
       for (int e = 0; e < VEC; ++e) ll.set(c * VEC + e, pk.e[e]);
@@ -516,15 +567,15 @@ __global__ void __launch_bounds__(kRowCTA, 1)
       if (active && tl == 0) scales[(b * s + l) * lines + line] = sc;
     };
     // slices are stored VEC elements at a time
-    Pack<ST, VEC> pq;
+    QT pq[VEC];
     ST *dl = dst;
     int cur_l = -1;
-    auto emit = [&](int l, int i, ST q) {
+    auto emit = [&](int l, int i, QT q) {
       if (l != cur_l) { dl = dst + l * level_stride; cur_l = l; }
-      pq.e[i % VEC] = q;
+      pq[i % VEC] = q;
       if (i % VEC == VEC - 1) {
         const int c = i / VEC;
-        if ((wmask >> c) & 1) *reinterpret_cast<Pack<ST, VEC> *>(dl + c * T * VEC) = pq;
+        if ((wmask >> c) & 1) store_slices<SK, VEC>(dl + c * T * VEC, pq);
       }
     };
     ll.run(s, alpha, reduce, emit, put_scale, [](int) {});
@@ -646,8 +697,8 @@ __global__ void __launch_bounds__(kColCTA, 1)
       if (rank == 0 && g == 0 && col_ok) scales[((int64_t)b * s + l) * lines + n] = sc;
     };
     Pack<ST, 4> pq;
-    auto emit = [&](int l, int i, ST q) {
-      pq.e[i & 3] = q;
+    auto emit = [&](int l, int i, typename QOut<SK>::type q) {
+      pq.e[i & 3] = to_slice<SK>(q);
       if ((i & 3) == 3)
         *reinterpret_cast<Pack<ST, 4> *>(outst + c * PITCH + 4 * (g + G * (i >> 2)) * sizeof(ST)) =
             pq;
@@ -784,12 +835,14 @@ template <typename TIn, int SK, bool EXACT>
 int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K, int ld,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
   using ST = typename SliceT<SK>::type;
-  constexpr int VEC = 16 / (int)sizeof(TIn);
+  constexpr int VEC = row_vec<TIn>();
   *done = false;
   // bulk copies need 16-byte aligned rows whose size is a multiple of 16
+  // (a last chunk that straddles K is read element by element)
   const bool ok = ((uintptr_t)in % 16 == 0) && (sl * (int64_t)sizeof(TIn)) % 16 == 0 &&
-                  (sb * (int64_t)sizeof(TIn)) % 16 == 0 && K % VEC == 0 && K > 0 &&
-                  ld % VEC == 0 && ((int64_t)ld * (int64_t)sizeof(ST)) % 16 == 0;
+                  (sb * (int64_t)sizeof(TIn)) % 16 == 0 &&
+                  (K * (int64_t)sizeof(TIn)) % 16 == 0 && K > 0 && ld % VEC == 0 &&
+                  ((int64_t)ld * (int64_t)sizeof(ST)) % 16 == 0;
   if (!ok) return OZ_OK;
   const int rowp = (K * (int)sizeof(TIn) + 127) / 128 * 128;
   auto go = [&](auto t_tag, auto nc_tag) -> int {

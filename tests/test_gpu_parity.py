@@ -89,7 +89,7 @@ COMBOS = [(ik, sk) for ik in ("fp64", "fp32", "fp16", "bf16") for sk in ("int8",
 
 
 @pytest.mark.parametrize("ik,sk", COMBOS)
-@pytest.mark.parametrize("K", [1, 37, 256, 1000, 4096])
+@pytest.mark.parametrize("K", [1, 37, 256, 1000, 1002, 4096])
 def test_split_rows_all_dtypes(ik, sk, K):
     rng = np.random.default_rng(K * 31 + len(ik) * 7 + len(sk))
     x = rand_lines(rng, (2, 19, K), ik)
