@@ -63,11 +63,12 @@ class Backend:
     def gemm(self, a_sl, b_sl, a_sc, b_sc, batch: int, m: int, n: int, k: int, num_splits: int,
              out_dtype: torch.dtype, skip_tail: bool, a_idx=None, b_idx=None,
              out: Optional[torch.Tensor] = None, col0: int = 0,
-             b_block_cols: int = 0) -> torch.Tensor:
+             b_block_cols: int = 0, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """C (batch, m, n); with ``out`` (batch, m, N_total) the result is written
         into its columns [col0, col0 + n) instead.  With ``b_block_cols`` the B
         slices are (BB, blocks, s, b_block_cols, ld) and their scales
-        (BB, blocks, s, b_block_cols): column blocks as a gather produces them."""
+        (BB, blocks, s, b_block_cols): column blocks as a gather produces them.
+        ``stream``: launch there instead of on the current stream."""
         c = torch.empty((batch, m, n), dtype=out_dtype, device=a_sl.device) if out is None else out
         if batch == 0 or m == 0 or n == 0:
             return c
@@ -78,7 +79,7 @@ class Backend:
             a_idx.data_ptr() if a_idx is not None else None,
             b_idx.data_ptr() if b_idx is not None else None, a_sl.shape[0], b_sl.shape[0],
             b_block_cols, ptr, c.stride(-2), _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
-            torch.cuda.current_stream(a_sl.device).cuda_stream))
+            (stream or torch.cuda.current_stream(a_sl.device)).cuda_stream))
         return c
 
 
@@ -263,6 +264,23 @@ class PeerBlocks:
         self.copy_streams = []
         self.gemm_streams = []
         self.calls = 0
+        # per buffer set: block views, and (dst, src) byte addresses of every
+        # peer block's slices and scales
+        self.blocks = []
+        for par in range(2):
+            sl, sc = self.sl[par], self.sc[par]
+            bsl = sl[0, 0].numel() * sl.element_size()
+            bsc = sc[0, 0].numel() * 4
+            views = [(sl[:, j:j + 1], sc[:, j:j + 1]) for j in range(self.world)]
+            copies = {}
+            for q in range(self.world):
+                if q != self.rank:
+                    copies[q] = (sl[0, q].data_ptr(), self.peer[(q, par)][0] + q * bsl, bsl,
+                                 sc[0, q].data_ptr(), self.peer[(q, 2 + par)][0] + q * bsc, bsc)
+            self.blocks.append((views, copies))
+        self.ready = torch.cuda.Event()
+        self.a_ready = torch.cuda.Event()
+        self.arrived = [torch.cuda.Event() for _ in range(self.world)]
 
     def streams(self, copies: int, gemms: int):
         while len(self.copy_streams) < copies:
@@ -280,11 +298,13 @@ class PeerBlocks:
 
 _PEER_CACHE: Dict[tuple, PeerBlocks] = {}
 
-# streams of the p2p transport: copies in flight at once (blocks arrive one
-# after another, so the first block GEMMs start early) and streams the block
-# GEMMs run on (None = one per peer block: every arrived block may start)
-P2P_COPY_STREAMS = 2
-P2P_GEMM_STREAMS: Optional[int] = None
+# streams of the p2p transport: copy streams (blocks arrive one after another,
+# so the first block GEMMs start early) and streams the block GEMMs run on
+# (None = one per peer block).  Measured on 8 B200s at 8192^3: 1 copy stream
+# and 2 GEMM streams were fastest (besides the current stream, which runs
+# the GEMM of the rank's own block).
+P2P_COPY_STREAMS = 1
+P2P_GEMM_STREAMS: Optional[int] = 2
 
 
 def release_peer_buffers(group=None) -> None:
@@ -307,7 +327,12 @@ def _peer_blocks(group, shape_sl, shape_sc, slice_dtype, dev) -> PeerBlocks:
 
 def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode, n, w, ld,
                  skip_tail, group):
-    """Pipelined gather: every block GEMM starts as soon as its block is here."""
+    """Pipelined gather: every block GEMM starts as soon as its block is here.
+
+    Host work per call is kept small (views, addresses and events are cached
+    in the PeerBlocks), since at 8 GPUs a whole call takes about a millisecond
+    of device time.
+    """
     dev = A_local.device
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     m_loc, k = A_local.shape
@@ -316,6 +341,7 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
     par = pb.calls % 2
     pb.calls += 1
     sl, sc = pb.sl[par], pb.sc[par]
+    views, copies = pb.blocks[par]
     cur = torch.cuda.current_stream(dev)
     _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, sl[0, rank],
                  sc[0, rank])
@@ -323,51 +349,45 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
     # set this call reuses (its copies of two calls ago ended before it
     # entered this all-reduce)
     dist.all_reduce(pb.flag, group=group)
-    ready = torch.cuda.Event()
-    ready.record(cur)
+    pb.ready.record(cur)
     A3 = A_local.reshape(1, m_loc, k)
     a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
                                slice_dtype, mode)
-    a_ready = torch.cuda.Event()
-    a_ready.record(cur)
+    pb.a_ready.record(cur)
     blocks = -(-n // w)
-    order = [(rank + d) % world for d in range(1, world)]
-    order = [j for j in order if j < blocks]
+    order = [j for j in ((rank + d) % world for d in range(1, world)) if j < blocks]
     copy_streams, gemm_streams = pb.streams(
         max(1, P2P_COPY_STREAMS), max(1, P2P_GEMM_STREAMS or len(order)))
     lib = _lib.load()
-    blk_sl = sl[0, 0].numel() * sl.element_size()
-    blk_sc = sc[0, 0].numel() * 4
-    arrived = {}
+    for cs in copy_streams:
+        cs.wait_event(pb.ready)
     for i, j in enumerate(order):
         cs = copy_streams[i % len(copy_streams)]
-        cs.wait_event(ready)
-        src_sl = pb.peer[(j, par)][0] + j * blk_sl
-        src_sc = pb.peer[(j, 2 + par)][0] + j * blk_sc
-        _lib.check(lib.oz_copy_async(sl[0, j].data_ptr(), src_sl, blk_sl, cs.cuda_stream))
-        _lib.check(lib.oz_copy_async(sc[0, j].data_ptr(), src_sc, blk_sc, cs.cuda_stream))
-        ev = torch.cuda.Event()
-        ev.record(cs)
-        arrived[j] = ev
+        d_sl, s_sl, n_sl, d_sc, s_sc, n_sc = copies[j]
+        _lib.check(lib.oz_copy_async(d_sl, s_sl, n_sl, cs.cuda_stream))
+        _lib.check(lib.oz_copy_async(d_sc, s_sc, n_sc, cs.cuda_stream))
+        pb.arrived[j].record(cs)
     c = torch.empty((1, m_loc, n), dtype=A_local.dtype, device=dev)
 
-    def block_gemm(j):
+    def block_gemm(j, stream):
+        b_sl, b_sc = views[j]
         c0, c1 = j * w, min(n, (j + 1) * w)
-        backend.gemm(a_sl, sl[:, j:j + 1], a_sc, sc[:, j:j + 1], 1, m_loc, c1 - c0, k,
-                     num_splits, A_local.dtype, skip_tail, out=c, col0=c0, b_block_cols=w)
+        backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, c1 - c0, k, num_splits, A_local.dtype,
+                     skip_tail, out=c, col0=c0, b_block_cols=w, stream=stream)
 
     if rank < blocks:
-        block_gemm(rank)
+        block_gemm(rank, cur)
+    for gs in gemm_streams:
+        gs.wait_event(pb.a_ready)
     for i, j in enumerate(order):
         gs = gemm_streams[i % len(gemm_streams)]
-        gs.wait_event(a_ready)
-        gs.wait_event(arrived[j])
-        with torch.cuda.stream(gs):
-            block_gemm(j)
+        gs.wait_event(pb.arrived[j])
+        block_gemm(j, gs)
+    # the current stream joins every GEMM stream before anything else runs on
+    # it, so c, a_sl and a_sc (allocated on it) are not reused while the side
+    # streams still read or write them
     for gs in gemm_streams:
         cur.wait_stream(gs)
-        for t in (c, a_sl, a_sc):
-            t.record_stream(gs)
     return c
 
 
@@ -393,7 +413,7 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
     * ``"p2p"`` (NCCL groups of one process per GPU): every rank maps its
       peers' slice buffers once (CUDA IPC) and pulls block after block with
       copy-engine copies; the GEMM of each block starts as soon as it has
-      arrived, on a stream of its own, so the transfer overlaps the GEMMs.
+      arrived (on one of two streams), so the transfer overlaps the GEMMs.
     """
     backend = backend or Backend()
     dev = A_local.device

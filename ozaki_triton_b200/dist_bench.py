@@ -52,20 +52,16 @@ def main(args):
     gemm_ms = []
 
     class TimedBackend(ozd.Backend):
-        """Brackets every GEMM launch with events on the stream it runs on."""
+        """Records an event before the first GEMM launch of a step."""
         record = False
+        first = None
 
         def gemm(self, *a, **kw):
-            if not self.record:
-                return super().gemm(*a, **kw)
-            st = torch.cuda.current_stream()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            c = super().gemm(*a, **kw)
-            e1.record(st)
-            gemm_ms.append((e0, e1))
-            return c
+            if self.record and self.first is None:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(kw.get("stream") or torch.cuda.current_stream())
+                self.first = e0
+            return super().gemm(*a, **kw)
 
     be = TimedBackend()
 
@@ -80,7 +76,15 @@ def main(args):
         return ozd.ozaki_matmul_mrows(a_dev, b_dev, S, torch.int8, backend=be, b_blocks=b_blocks)
 
     def step():
-        return run(a_loc, b)
+        c = run(a_loc, b)
+        if be.record and be.first is not None:
+            # the GEMM phase of a step: its first GEMM launch to the join of
+            # every GEMM stream (the block GEMMs of the p2p transport overlap)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            gemm_ms.append((be.first, e1))
+            be.first = None
+        return c
 
     for _ in range(args.warmup):
         step()
@@ -100,14 +104,7 @@ def main(args):
     t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    # GEMM time of a step: from its first GEMM launch's start to the last end
-    # (the block GEMMs of the p2p transport overlap on two streams)
-    per_step = len(gemm_ms) // args.steps
-    spans = []
-    for i in range(args.steps):
-        calls = gemm_ms[i * per_step:(i + 1) * per_step]
-        first = calls[0][0]
-        spans.append(max(first.elapsed_time(e1) for _, e1 in calls))
+    spans = [e0.elapsed_time(e1) for e0, e1 in gemm_ms]
     g_local = statistics.mean(spans)
 
     # end to end through the public sharded call with host operands: each
@@ -177,7 +174,8 @@ def main(args):
             "clocks": clk.summary(),
             # rank 0's own kernels per step: transpose + split of B's panel (or
             # blocks), split of A's rows, the GEMM (NCCL kernels not counted)
-            "gpu_launches": ((3 + per_step) if sharded else 2 + 2 * (b_blocks or 4)) * args.steps,
+            "gpu_launches": ((3 + (world if args.transport == "p2p" else 1)) if sharded
+                             else 2 + 2 * (b_blocks or 4)) * args.steps,
             "e2e": e2e,
         }
         print(json.dumps(line), flush=True)
