@@ -238,29 +238,49 @@ class PeerBlocks:
     def __init__(self, group, shape_sl, shape_sc, slice_dtype, dev):
         lib = _lib.load()
         self.group = group
+        self.dev = dev
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.sl = [torch.empty(shape_sl, dtype=slice_dtype, device=dev) for _ in range(2)]
         self.sc = [torch.empty(shape_sc, dtype=torch.float32, device=dev) for _ in range(2)]
         self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        # Every rank takes the same collective steps whatever fails locally:
+        # a failed export sends None, a failed import is counted, and one
+        # all-reduce decides for all ranks whether the mappings are usable.
+        self.error = ""
         mine = []
         for t in self.sl + self.sc:
             h = ctypes.create_string_buffer(_lib.OZ_IPC_HANDLE_BYTES)
             off = ctypes.c_int64()
-            _lib.check(lib.oz_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
+            if lib.oz_ipc_export(t.data_ptr(), h, ctypes.byref(off)) != _lib.OZ_OK:
+                self.error = lib.oz_last_error().decode(errors="replace")
+                mine = None
+                break
             mine.append((h.raw, off.value))
         torch.cuda.synchronize(dev)
         everyone = [None] * self.world
         dist.all_gather_object(everyone, mine, group=group)
         self.peer: Dict[Tuple[int, int], Tuple[int, int]] = {}
+        ok = all(e is not None for e in everyone)
+        if not ok and not self.error:
+            self.error = "a peer could not export its buffers"
         for q in range(self.world):
-            if q == self.rank:
+            if q == self.rank or not ok:
                 continue
             for i, (h, off) in enumerate(everyone[q]):
                 ptr = ctypes.c_void_p()
-                _lib.check(lib.oz_ipc_import(h, off, ctypes.byref(ptr)))
+                if lib.oz_ipc_import(h, off, ctypes.byref(ptr)) != _lib.OZ_OK:
+                    self.error = lib.oz_last_error().decode(errors="replace")
+                    ok = False
+                    break
                 self.peer[(q, i)] = (ptr.value, off)
-        self.dev = dev
+        agree = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=group)
+        self.usable = bool(agree.item())
+        if not self.usable:
+            self.close()
+            self.sl, self.sc = [], []
+            return
         self.copy_streams = []
         self.gemm_streams = []
         self.calls = 0
@@ -307,11 +327,20 @@ P2P_COPY_STREAMS = 1
 P2P_GEMM_STREAMS: Optional[int] = 2
 
 
+def p2p_status(group=None) -> str:
+    """"ok", "unused" or why the p2p transport fell back to the all-gather."""
+    pbs = [pb for k, pb in _PEER_CACHE.items() if k[0] == id(group)]
+    if not pbs:
+        return "unused"
+    bad = [pb.error or "unusable" for pb in pbs if not pb.usable]
+    return bad[0] if bad else "ok"
+
+
 def release_peer_buffers(group=None) -> None:
     """Unmap and free the cached peer buffers (collective: every rank calls it)."""
     for key in [k for k in _PEER_CACHE if k[0] == id(group)]:
         pb = _PEER_CACHE.pop(key)
-        torch.cuda.synchronize(pb.sl[0].device)
+        torch.cuda.synchronize(pb.dev)
         dist.barrier(group=group)          # no peer copies from our buffers any more
         pb.close()
         dist.barrier(group=group)          # every peer has unmapped them
@@ -331,13 +360,16 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
 
     Host work per call is kept small (views, addresses and events are cached
     in the PeerBlocks), since at 8 GPUs a whole call takes about a millisecond
-    of device time.
+    of device time.  Returns None, on every rank alike, when the peer
+    mappings could not be set up (the caller then uses the all-gather).
     """
     dev = A_local.device
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     m_loc, k = A_local.shape
     pb = _peer_blocks(group, (1, world, num_splits, w, ld), (1, world, num_splits, w),
                       slice_dtype, dev)
+    if not pb.usable:
+        return None
     par = pb.calls % 2
     pb.calls += 1
     sl, sc = pb.sl[par], pb.sc[par]
@@ -414,6 +446,8 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
       peers' slice buffers once (CUDA IPC) and pulls block after block with
       copy-engine copies; the GEMM of each block starts as soon as it has
       arrived (on one of two streams), so the transfer overlaps the GEMMs.
+      If the mappings cannot be set up on some rank, every rank uses the
+      collective transport instead (``p2p_status`` reports why).
     """
     backend = backend or Backend()
     dev = A_local.device
@@ -441,7 +475,8 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
     if transport == "p2p" and world > 1 and n > 0:
         c = _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode, n, w,
                          ld, skip_tail, group)
-        return c.reshape(m_loc, n)
+        if c is not None:
+            return c.reshape(m_loc, n)
     # one block per rank (blocks past ceil(n / w) stay empty and are not read)
     b_sl, b_sc = _blocked_buffers(world, num_splits, w, ld, slice_dtype, dev)
     _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, b_sl[0, rank],

@@ -164,6 +164,9 @@ def main(args):
                                        "from rank 0 over NCCL in column blocks"),
                        "rows_per_rank": rows,
                        "b_panel_cols": ozd.block_width(N, world) if sharded else None,
+                       "transport": (args.transport + (" (" + ozd.p2p_status() + ")"
+                                                       if args.transport == "p2p" else ""))
+                       if sharded else "broadcast",
                        "b_blocks": None if sharded else (b_blocks or "auto")},
             "roofline": {"bound": "tensor",
                          "kernel": "cross_gemm_kernel (rank 0 rows; span of the step's GEMMs)",
@@ -174,7 +177,7 @@ def main(args):
             "clocks": clk.summary(),
             # rank 0's own kernels per step: transpose + split of B's panel (or
             # blocks), split of A's rows, the GEMM (NCCL kernels not counted)
-            "gpu_launches": ((3 + (world if args.transport == "p2p" else 1)) if sharded
+            "gpu_launches": ((3 + (world if ozd.p2p_status() == "ok" else 1)) if sharded
                              else 2 + 2 * (b_blocks or 4)) * args.steps,
             "e2e": e2e,
         }
