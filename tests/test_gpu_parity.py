@@ -351,17 +351,20 @@ def test_gemm_column_blocked_b_bit_identical(n, w, sk, tile, monkeypatch):
 
 
 @pytest.mark.parametrize("use_ws", [False, True])
-@pytest.mark.parametrize("ik,sk,K", [("fp64", "int8", 8192), ("fp64", "int8", 300),
-                                     ("fp32", "fp16", 1000), ("bf16", "int8", 2048),
-                                     ("fp64", "fp32", 77)])
-def test_split_columns_c_abi_workspace_and_cluster(use_ws, ik, sk, K):
+@pytest.mark.parametrize("ik,sk,K,N", [("fp64", "int8", 8192, 70), ("fp64", "int8", 300, 70),
+                                       ("fp32", "fp16", 1000, 70), ("bf16", "int8", 2048, 70),
+                                       ("fp64", "fp32", 77, 70), ("fp32", "fp16", 1000, 64),
+                                       ("fp32", "int8", 16384, 64), ("bf16", "fp16", 512, 64)])
+def test_split_columns_c_abi_workspace_and_cluster(use_ws, ik, sk, K, N):
     """Columns of a row-major matrix through the C ABI: oz_split (cluster
-    kernel, no scratch) and oz_split_ex with the transpose workspace give the
-    same bits as the oracle."""
+    kernel where the layout allows it, no scratch) and oz_split_ex (fp32/fp16/
+    bf16: the cluster kernel where it applies, else the transpose workspace;
+    fp64: the workspace) give the same bits as the oracle.  N = 70 rows are
+    not 16-byte aligned for fp32 (no cluster kernel); K = 16384 fp32 exceeds
+    the cluster's reach (transpose path)."""
     from ozaki_triton_b200 import _lib
     from ozaki_triton_b200.api import _OZ_DTYPE
     rng = np.random.default_rng(K + len(ik))
-    N = 70
     b = rand_lines(rng, (2, N, K), ik)
     bd = to_dev(np.ascontiguousarray(np.swapaxes(b, -1, -2)), ik)     # (2, K, N) row-major
     lines_np = np.swapaxes(host(bd).astype(np.float64 if ik == "fp64" else np.float32), -1, -2)
