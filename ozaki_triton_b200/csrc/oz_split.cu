@@ -247,8 +247,14 @@ __device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv
   double qd;
   typename QOut<SK>::type q;
   if constexpr (SK == OZ_I8) {
+    // the reference's fp64 t = x +- 0.5 (rounded), then trunc(t) =
+    // sign(x) * floor(|t|) with floor(|t|) from the magic add rounded toward
+    // zero: fl_rz(|t| + 1.5 * 2^52) = 1.5 * 2^52 + floor(|t|), whose low word
+    // is floor(|t|) (no conversion instruction)
     const double t = __dadd_rn(x, copysign(0.5, x));
-    const int n = clamp_i8(__double2int_rz(t));
+    const int qa = __double2loint(__dadd_rz(fabs(t), 6755399441055744.0));
+    const int sgn = __double2hiint(x) >> 31;
+    const int n = clamp_i8((qa ^ sgn) - sgn);
     q = (uint32_t)n;
     qd = int_to_double_exact(n);
   } else {
@@ -426,6 +432,23 @@ constexpr int kRowCTA = 512;
 constexpr int kRowMaxStages = 4;
 constexpr int kRowSmem = 200 * 1024;
 
+// (batch, line) of a flat row index without a 64-bit division where that is
+// avoidable (a 64-bit division is a long instruction sequence, paid per row)
+__device__ __forceinline__ void row_coords(int64_t row, int lines, bool one_batch, int64_t &b,
+                                           int64_t &line) {
+  if (one_batch) {
+    b = 0;
+    line = row;
+  } else if (row <= (int64_t)0xFFFFFFFFu) {
+    const uint32_t r = (uint32_t)row, q = r / (uint32_t)lines;
+    b = q;
+    line = r - q * (uint32_t)lines;
+  } else {
+    b = row / lines;
+    line = row - b * lines;
+  }
+}
+
 // Elements per thread and chunk of the row kernel: 16-byte chunks of the
 // input, except fp64, whose 32-byte chunks (two 16-byte reads) give int8
 // slices 4-byte stores.
@@ -481,12 +504,13 @@ __global__ void __launch_bounds__(kRowCTA, 1)
   const int64_t groups = (total + RPS - 1) / RPS;
   const uint32_t row_bytes = (uint32_t)K * (uint32_t)sizeof(TIn);
 
+  const bool one_batch = total == lines;
   auto issue = [&](int64_t g, int st) {
     int nrows = (int)min((int64_t)RPS, total - g * RPS);
     mbar_arrive_expect_tx(&full[st], (uint32_t)nrows * row_bytes);
     for (int r = 0; r < nrows; ++r) {
-      const int64_t row = g * RPS + r;
-      const int64_t b = row / lines, line = row % lines;
+      int64_t b, line;
+      row_coords(g * RPS + r, lines, one_batch, b, line);
       bulk_load(smem + st * stage + r * rowp, in + b * stride_b + line * stride_line, row_bytes,
                 &full[st]);
     }
@@ -543,7 +567,8 @@ __global__ void __launch_bounds__(kRowCTA, 1)
       const int64_t gn = g + (int64_t)NS * gridDim.x;
       if (gn < groups) issue(gn, st);
     }
-    const int64_t b = active ? row / lines : 0, line = active ? row % lines : 0;
+    int64_t b = 0, line = 0;
+    if (active) row_coords(row, lines, one_batch, b, line);
     ST *dst = out + (b * s * lines + line) * (int64_t)ld + tl * VEC;
     const uint32_t wmask = active ? in_ld : 0u;
     const int64_t level_stride = (int64_t)lines * ld;
@@ -563,15 +588,15 @@ __global__ void __launch_bounds__(kRowCTA, 1)
       }
       return m;
     };
-    auto put_scale = [&](int l, float sc) {
-      if (active && tl == 0) scales[(b * s + l) * lines + line] = sc;
-    };
-    // slices are stored VEC elements at a time
+    // slices are stored VEC elements at a time, to dl = this level's row
     QT pq[VEC];
     ST *dl = dst;
-    int cur_l = -1;
+    auto put_scale = [&](int l, float sc) {
+      if (active && tl == 0) scales[(b * s + l) * lines + line] = sc;
+      dl = dst + l * level_stride;
+    };
     auto emit = [&](int l, int i, QT q) {
-      if (l != cur_l) { dl = dst + l * level_stride; cur_l = l; }
+      (void)l;
       pq[i % VEC] = q;
       if (i % VEC == VEC - 1) {
         const int c = i / VEC;
