@@ -206,7 +206,12 @@ def _cast_out(out: np.ndarray, out_kind: str) -> np.ndarray:
     if out_kind == "bf16":
         return round_to_bf16(out)
     if out_kind == "int8":
-        return np.trunc(out).astype(np.int64).astype(np.int8)
+        # ozaki_triton.py:452 casts the fp32 accumulator to the int8 output.
+        # Inside [-128, 127] that is truncation toward zero on every backend;
+        # outside it the GPU conversion saturates (the interpreter's numpy
+        # cast wraps), and this restatement follows the GPU: saturate, NaN -> 0.
+        t = np.trunc(np.nan_to_num(out.astype(np.float64), nan=0.0))
+        return np.clip(t, -128, 127).astype(np.int8)
     raise ValueError(out_kind)
 
 

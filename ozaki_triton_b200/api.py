@@ -39,8 +39,9 @@ SLICE_DTYPE_INFO = {
     torch.int8: (7, True),
 }
 
-# ozaki_triton.py:43-49 -- accepted input dtypes
-INPUT_DTYPES = {torch.float64, torch.float32, torch.float16, torch.bfloat16}
+# ozaki_triton.py:43-49 -- accepted input dtypes (int8 inputs are split like
+# fp32 ones and give an int8 C, truncated toward zero and saturated)
+INPUT_DTYPES = {torch.float64, torch.float32, torch.float16, torch.bfloat16, torch.int8}
 
 MAX_SPLITS = 8
 

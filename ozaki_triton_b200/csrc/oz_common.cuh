@@ -75,6 +75,10 @@ template <> struct InTraits<__half> {
   static __device__ __forceinline__ double to_double(__half v) { return (double)__half2float(v); }
   static __device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
 };
+template <> struct InTraits<int8_t> {
+  static __device__ __forceinline__ double to_double(int8_t v) { return (double)v; }
+  static __device__ __forceinline__ float to_float(int8_t v) { return (float)v; }
+};
 template <> struct InTraits<__nv_bfloat16> {
   static __device__ __forceinline__ double to_double(__nv_bfloat16 v) {
     return (double)__bfloat162float(v);

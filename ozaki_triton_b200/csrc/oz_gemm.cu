@@ -79,6 +79,7 @@ template <> struct OutT<OZ_F64> { using acc = double; using store = double; };
 template <> struct OutT<OZ_F32> { using acc = float; using store = float; };
 template <> struct OutT<OZ_F16> { using acc = float; using store = __half; };
 template <> struct OutT<OZ_BF16> { using acc = float; using store = __nv_bfloat16; };
+template <> struct OutT<OZ_I8> { using acc = float; using store = int8_t; };
 
 template <typename ACC> __device__ __forceinline__ ACC acc_add(ACC a, float v);
 template <> __device__ __forceinline__ double acc_add<double>(double a, float v) {
@@ -92,7 +93,11 @@ template <int OUTK> __device__ __forceinline__ typename OutT<OUTK>::store
 to_out(typename OutT<OUTK>::acc v) {
   if constexpr (OUTK == OZ_F16) return __float2half_rn(v);
   else if constexpr (OUTK == OZ_BF16) return __float2bfloat16_rn(v);
-  else return v;
+  else if constexpr (OUTK == OZ_I8) {
+    // int8 inputs give an int8 result: truncation toward zero, saturated to
+    // [-128, 127], NaN -> 0 (the GPU's float-to-int8 conversion)
+    return (int8_t)max(-128, min(127, __float2int_rz(v)));
+  } else return v;
 }
 
 // tile t -> (batch b, row tile mb, column tile nb) in a grouped raster:
@@ -510,6 +515,7 @@ int launch_out(int out_dtype, const CUtensorMap &ta, const CUtensorMap &tb, cons
     case OZ_F32: return launch_gemm<KIND, OZ_F32, NT, PAIR>(ta, tb, p, st);
     case OZ_F16: return launch_gemm<KIND, OZ_F16, NT, PAIR>(ta, tb, p, st);
     case OZ_BF16: return launch_gemm<KIND, OZ_BF16, NT, PAIR>(ta, tb, p, st);
+    case OZ_I8: return launch_gemm<KIND, OZ_I8, NT, PAIR>(ta, tb, p, st);
   }
   return set_error(OZ_ERR_UNSUPPORTED, "unsupported output dtype %d", out_dtype);
 }
@@ -563,7 +569,8 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   if (slice_dtype != OZ_I8 && slice_dtype != OZ_F16 && slice_dtype != OZ_BF16 &&
       slice_dtype != OZ_F32)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported slice dtype %d", slice_dtype);
-  if (out_dtype != OZ_F64 && out_dtype != OZ_F32 && out_dtype != OZ_F16 && out_dtype != OZ_BF16)
+  if (out_dtype != OZ_F64 && out_dtype != OZ_F32 && out_dtype != OZ_F16 && out_dtype != OZ_BF16 &&
+      out_dtype != OZ_I8)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported output dtype %d", out_dtype);
   if (flags & ~OZ_GEMM_SKIP_TAIL) return set_error(OZ_ERR_INVALID, "unknown flags 0x%x", flags);
   if (b_block_cols < 0 || (b_block_cols > 0 && b_block_cols < n && b_block_cols % 128 != 0))

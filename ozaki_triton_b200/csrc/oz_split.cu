@@ -1068,6 +1068,29 @@ int transpose_into(const void *in, int64_t batch, int64_t lines, int64_t k, int6
   return check_cuda(cudaGetLastError(), "transpose_lines launch");
 }
 
+// int8 inputs (accepted by the reference, ozaki_triton.py:43-49; an fp32
+// residual like every non-fp64 input) take the generic kernel: a rare input
+// type that does not need its own streaming instantiations.
+int dispatch_int8_input(int slice_dtype, const void *in_v, int64_t batch, int64_t lines,
+                        int64_t K, int64_t sb, int64_t sl, int64_t sk, int s, int alpha,
+                        void *slices, int64_t ld, float *scales, cudaStream_t st) {
+  const int8_t *in = reinterpret_cast<const int8_t *>(in_v);
+  dim3 grid((unsigned)lines, (unsigned)batch);
+#define OZ_A(SK)                                                                             \
+  split_any_kernel<int8_t, SK, false><<<grid, kAnyThreads, 0, st>>>(                          \
+      in, sb, sl, sk, (int)lines, (int)K, (int)ld, s, alpha,                                  \
+      reinterpret_cast<typename SliceT<SK>::type *>(slices), scales);                         \
+  break;
+  switch (slice_dtype) {
+    case OZ_I8: OZ_A(OZ_I8)
+    case OZ_F16: OZ_A(OZ_F16)
+    case OZ_BF16: OZ_A(OZ_BF16)
+    default: OZ_A(OZ_F32)
+  }
+#undef OZ_A
+  return check_cuda(cudaGetLastError(), "split_any_kernel launch");
+}
+
 int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
                int64_t stride_b, int64_t stride_line, int64_t stride_k, int32_t num_splits,
                int32_t alpha, int slice_dtype, int residual_mode, void *slices, int64_t ld,
@@ -1085,7 +1108,8 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
   // int8 slices saturate at 2^7 anyway; the rounding needs |x| < 2^22
   if (slice_dtype == OZ_I8 && alpha > 21)
     return set_error(OZ_ERR_INVALID, "alpha %d too large for int8 slices (at most 21)", alpha);
-  if (in_dtype != OZ_F64 && in_dtype != OZ_F32 && in_dtype != OZ_F16 && in_dtype != OZ_BF16)
+  if (in_dtype != OZ_F64 && in_dtype != OZ_F32 && in_dtype != OZ_F16 && in_dtype != OZ_BF16 &&
+      in_dtype != OZ_I8)
     return set_error(OZ_ERR_UNSUPPORTED, "unsupported input dtype %d", in_dtype);
   if (residual_mode != OZ_RESIDUAL_COMPAT && residual_mode != OZ_RESIDUAL_EXACT)
     return set_error(OZ_ERR_INVALID, "unknown residual mode %d", residual_mode);
@@ -1145,6 +1169,9 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
     }
   }
   switch (in_dtype) {
+    case OZ_I8:
+      return dispatch_int8_input(slice_dtype, in, batch, lines, k, stride_b, stride_line,
+                                 stride_k, num_splits, alpha, slices, ld, scales, st);
     case OZ_F64:
       return dispatch_slice<double>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
                                     stride_line, stride_k, num_splits, alpha, slices, ld, scales, st);

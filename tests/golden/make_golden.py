@@ -120,13 +120,25 @@ def main(ref_dir: str):
         ("cols_f64_i8_s4", "fp64", "int8", 4, 2, 70, 260, "cols"),
         ("cols_f32_f16_s2", "fp32", "fp16", 2, 1, 40, 129, "cols"),
         ("cols_f64_f16_s3", "fp64", "fp16", 3, 1, 33, 1040, "cols"),
+        # int8 inputs (accepted by ozaki_triton.py:43-49); drawn from their own
+        # generator so that the cases above keep their inputs
+        ("rows_i8_i8_s2", "int8", "int8", 2, 1, 12, 96, "rows"),
+        ("rows_i8_f32_s1", "int8", "fp32", 1, 1, 8, 64, "rows"),
+        ("cols_i8_f16_s3", "int8", "fp16", 3, 1, 24, 80, "cols"),
     ]
+    rng_i8 = np.random.default_rng(8)
     for name, ik, sk, s, B, L, K, layout in split_cases:
-        x = spread(rng, (B, L, K))
-        sp = special_rows(rng, K, ik)
-        assert np.all(np.isfinite(torch.from_numpy(sp).to(tdt[ik]).double().numpy()))
-        n_sp = min(len(sp), L)
-        x[0, :n_sp] = sp[:n_sp]
+        if ik == "int8":
+            x = rng_i8.integers(-128, 128, (B, L, K)).astype(np.float64)
+            x[0, 0] = 0; x[0, 1] = -128; x[0, 2] = 127          # zero, clamp-edge rows
+            x[0, 3] = 0; x[0, 3, K // 2] = 5                     # single nonzero
+            x[0, 4] = np.where(np.arange(K) % 2 == 0, 1, -1)     # alternating signs
+        else:
+            x = spread(rng, (B, L, K))
+            sp = special_rows(rng, K, ik)
+            assert np.all(np.isfinite(torch.from_numpy(sp).to(tdt[ik]).double().numpy()))
+            n_sp = min(len(sp), L)
+            x[0, :n_sp] = sp[:n_sp]
         t = torch.from_numpy(x).to(tdt[ik])
         if layout == "cols":
             # store B as (B, K, N) and split its transposed view, as
@@ -164,9 +176,17 @@ def main(ref_dir: str):
         ("mm_f32_i8_s4", "fp32", "int8", 4, (40, 160), (160, 48), "c3"),
         ("mm_f16_f32_s1", "fp16", "fp32", 1, (48, 64), (64, 40), "normal"),
         ("mm_f64_i8_s2_k1", "fp64", "int8", 2, (17, 1), (1, 9), "normal"),
+        # int8 inputs and an int8 result: entries in [-3, 3] and K = 8 keep C
+        # inside the int8 range (the reference's out-of-range conversion
+        # depends on the backend)
+        ("mm_i8_i8_s2", "int8", "int8", 2, (24, 8), (8, 16), "int_small"),
+        ("mm_i8_f16_s1", "int8", "fp16", 1, (12, 6), (6, 10), "int_small"),
     ]
     for name, ik, sk, s, ash, bsh, law in mm_cases:
-        if law == "c3":
+        if law == "int_small":
+            a = rng_i8.integers(-3, 4, ash).astype(np.float64)
+            b = rng_i8.integers(-3, 4, bsh).astype(np.float64)
+        elif law == "c3":
             a = c3_dist(rng, ash); b = c3_dist(rng, bsh)
         elif law == "spread":
             a = spread(rng, ash); b = np.swapaxes(spread(rng, bsh[:-2] + (bsh[-1], bsh[-2])), -1, -2)

@@ -73,6 +73,8 @@ def np_input(x, kind):
         return x.astype(np.float16)
     if kind == "fp64":
         return x.astype(np.float64)
+    if kind == "int8":
+        return x.astype(np.int8)
     return x.astype(np.float32)   # fp32, bf16 (bf16 values carried in float32)
 
 

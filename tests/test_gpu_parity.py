@@ -298,6 +298,21 @@ def test_headline_size_properties():
     assert same_bits(c.cpu().numpy()[np.ix_(rows, cols)], want)
 
 
+def test_int8_inputs_saturate_out_of_range():
+    """int8 inputs (accepted by the reference) give an int8 C; results outside
+    [-128, 127] saturate like the GPU's float-to-int8 conversion."""
+    rng = np.random.default_rng(9)
+    a = rng.integers(-128, 128, (40, 64)).astype(np.int8)
+    b = rng.integers(-128, 128, (64, 24)).astype(np.int8)
+    for sk in ("int8", "fp16"):
+        c = oz.ozaki_matmul(to_dev(a, "int8"), to_dev(b, "int8"), num_splits=3,
+                            slice_dtype=TDT[sk])
+        assert c.dtype == torch.int8
+        want = oracle.ozaki_matmul(a, b, 3, sk, "int8")
+        assert same_bits(host(c), want)
+        assert (want == 127).any() and (want == -128).any()       # saturation exercised
+
+
 @pytest.mark.parametrize("tile", ["1,128", "2,128", "1,64", "2,64"])
 @pytest.mark.parametrize("s", [2, 4])
 def test_gemm_tile_configs_bit_identical(tile, s, monkeypatch):

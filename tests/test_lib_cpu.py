@@ -109,7 +109,7 @@ def test_argument_validation_without_launch():
     assert gemm(s=0) == _lib.OZ_ERR_INVALID
     assert gemm(s=9) == _lib.OZ_ERR_INVALID
     assert gemm(sd=_lib.OZ_F64) == _lib.OZ_ERR_UNSUPPORTED
-    assert gemm(od=_lib.OZ_I8) == _lib.OZ_ERR_UNSUPPORTED
+    assert gemm(od=7) == _lib.OZ_ERR_UNSUPPORTED
     assert gemm(batch=3) == _lib.OZ_ERR_INVALID          # 1 A batch for 3 outputs, no index
     assert gemm(ldc=2) == _lib.OZ_ERR_INVALID
     assert gemm(a=ctypes.c_void_p(17)) == _lib.OZ_ERR_INVALID   # misaligned slices
