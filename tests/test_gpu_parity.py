@@ -298,6 +298,25 @@ def test_headline_size_properties():
     assert same_bits(c.cpu().numpy()[np.ix_(rows, cols)], want)
 
 
+@pytest.mark.parametrize("sk,K,lines,s", [("int8", 1000, 63, 4), ("int8", 8192, 64, 4),
+                                          ("fp16", 2048, 33, 3), ("fp32", 4100, 10, 2),
+                                          ("bf16", 7, 5, 1)])
+@pytest.mark.parametrize("residual", ["compat", "exact"])
+def test_split_fp64_column_pairs(sk, K, lines, s, residual):
+    """fp64 columns of a row-major B through the column-pair kernel (no
+    transposed copy): an odd number of columns (the last panel's second
+    column lies past the view and is zero-filled), batch 2, K not a multiple
+    of the 2048-row chunk, every slice type, both residual modes."""
+    rng = np.random.default_rng(K + lines)
+    N = 64                                            # row pitch: 512 bytes
+    b = rand_lines(rng, (2, N, K), "fp64")
+    bd = to_dev(np.ascontiguousarray(np.swapaxes(b, -1, -2)), "fp64")   # (2, K, N)
+    view = bd[:, :, :lines].transpose(-1, -2)         # (2, lines, K), lines contiguous
+    lines_np = np.swapaxes(host(bd), -1, -2)[:, :lines]
+    alpha = oz.compute_split_bits(K, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    check_split(view, lines_np, s, alpha, sk, "fp64", residual=residual)
+
+
 def test_int8_inputs_saturate_out_of_range():
     """int8 inputs (accepted by the reference) give an int8 C; results outside
     [-128, 127] saturate like the GPU's float-to-int8 conversion."""
