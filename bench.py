@@ -59,18 +59,62 @@ def make_inputs(seed: int = 2, m: int = M, n: int = N, k: int = K):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """SM clock / clock-event-reason sampling during the timed region.
+
+    NVML (read-only queries) polled every 5 ms from a thread; nvidia-smi
+    -lms 50 where NVML cannot be loaded.  The GPU is found by its PCI bus id,
+    so CUDA_VISIBLE_DEVICES remapping does not matter.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.005
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self.samples = []            # (sm MHz, max MHz, reasons bitmask)
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:  # noqa: BLE001 - fall back to the index
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        return pynvml, h
+
+    def _poll(self):
+        pv, h = self.nvml
+        reasons = getattr(pv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = pv.nvmlDeviceGetMaxClockInfo(h, pv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                self.samples.append((pv.nvmlDeviceGetClockInfo(h, pv.NVML_CLOCK_SM), mx,
+                                     int(reasons(h))))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.PERIOD_S)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 5:
+                time.sleep(0.001)
+            self.samples.clear()
+            return self
+        except Exception:  # noqa: BLE001 - no NVML: nvidia-smi
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
@@ -92,6 +136,10 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,6 +151,20 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        if self.nvml is not None:
+            pv = self.nvml[0]
+            bits = [pv.nvmlClocksThrottleReasonHwSlowdown,
+                    pv.nvmlClocksThrottleReasonHwThermalSlowdown,
+                    pv.nvmlClocksThrottleReasonSwThermalSlowdown,
+                    pv.nvmlClocksThrottleReasonSwPowerCap]
+            for mhz, mxx, r in self.samples:
+                sm.append(float(mhz))
+                mx = float(mxx)
+                for nm, bit in zip(names, bits):
+                    if r & bit:
+                        reasons.add(nm)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml"}
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -216,6 +278,8 @@ def main():
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS),
                     help="benchmark configuration (C3 = the headline)")
     ap.add_argument("--num-splits", type=int, default=0, help="override the config's s")
+    ap.add_argument("--graph", action="store_true",
+                    help="1 GPU: time CUDA-graph replays of the step (launch-bound small configs)")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, DGEMM or CPU legs): the ncu command line")
     args = ap.parse_args()
@@ -310,18 +374,19 @@ def run_single(args):
         b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), Nn, Kk, s, alpha, sd, residual)
         a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), Mm, Kk, s, alpha, sd, residual)
         c = torch.empty((BN, Mm, Nn), dtype=dt, device=dev)
+        st = torch.cuda.current_stream()        # the capturing stream under --graph
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+            e0.record(st)
         _lib.check(_lib.load().oz_cross_gemm(
             a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), BN, Mm, Nn, Kk,
             a_sl.shape[-1], s, _OZ_DTYPE[sd], _OZ_DTYPE[dt],
             a_idx.data_ptr() if a_idx is not None else None,
             b_idx.data_ptr() if b_idx is not None else None, BA, BB, c.data_ptr(), Nn, 0,
-            stream.cuda_stream))
+            st.cuda_stream))
         if record:
-            e1.record(stream)
+            e1.record(st)
             gemm_events.append((e0, e1))
         return c
 
@@ -336,13 +401,35 @@ def run_single(args):
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    graph = None
+    if args.graph:
+        # the whole step (both splits and the GEMM) captured once and replayed:
+        # no host launch work per step (the GEMM time for the roofline comes
+        # from event-timed steps outside the graph)
+        for _ in range(3):
+            step(True)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        n0 = _lib.load().oz_launch_count()
+        with torch.cuda.graph(graph):
+            step(False)
+        graph_launches = _lib.load().oz_launch_count() - n0
+        torch.cuda.synchronize()
     with ClockSampler(0) as clk:
         torch.cuda.synchronize()
+        launches0 = _lib.load().oz_launch_count()
         start.record(stream)
         for _ in range(args.steps):
-            step(True)
+            if graph is not None:
+                graph.replay()
+            else:
+                step(True)
         end.record(stream)
         torch.cuda.synchronize()
+        # the library's own kernels in the timed region (counted at launch;
+        # a replayed graph launches the kernels it captured)
+        launches = (_lib.load().oz_launch_count() - launches0 if graph is None
+                    else graph_launches * args.steps)
     ms = start.elapsed_time(end) / args.steps
     gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
     flops = 2.0 * BN * Mm * Nn * Kk
@@ -416,7 +503,8 @@ def run_single(args):
                    "residual": "compat" if residual == _lib.OZ_RESIDUAL_COMPAT else "exact",
                    "l2": "no flush: operands larger than the 126 MB L2" if a.numel() * a.element_size() > 126e6
                    else "operands smaller than L2 (small config)",
-                   "parallelism": "1 GPU"},
+                   "parallelism": "1 GPU",
+                   "launch": "CUDA graph replay" if graph is not None else "eager"},
         "roofline": {"bound": "tensor", "kernel": f"cross_gemm_kernel<{SLICE_NAME[sd]}>",
                      "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
                      "frac": achieved / tensor_peak,
@@ -429,7 +517,7 @@ def run_single(args):
         "native_gemm_tflops": native_tflops,
         "native_gemm": "cuBLAS DGEMM" if dt == torch.float64 else "cuBLAS SGEMM (no TF32)",
         "clocks": clk.summary(),
-        "gpu_launches": (3 + (1 if BB * Nn * Kk > 0 else 0)) * args.steps,
+        "gpu_launches": launches,
         "e2e": e2e,
     }
     if not args.no_cpu_baseline and name == "C3":

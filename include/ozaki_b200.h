@@ -208,6 +208,11 @@ int oz_copy_async(void *dst, const void *src, int64_t bytes, void *stream);
  */
 int oz_device_status(void *stream, int32_t *code);
 
+/* Kernels the library has launched in this process, a running total (no
+ * counterpart in the reference; lets a caller count the device work of a
+ * region: the difference of two readings). */
+int64_t oz_launch_count(void);
+
 /* Message for the last error returned on the calling thread ("" if none). */
 const char *oz_last_error(void);
 

@@ -1,6 +1,7 @@
 // oz_api.cu -- library-wide C ABI entry points: error strings, the alpha
 // rule, device status and the version string.
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -20,6 +21,9 @@ int set_error(int code, const char *fmt, ...) {
   va_end(ap);
   return code;
 }
+
+static std::atomic<int64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int check_cuda(cudaError_t e, const char *what) {
   if (e == cudaSuccess) return OZ_OK;
@@ -67,3 +71,5 @@ extern "C" int oz_device_status(void *stream, int32_t *code) {
   if (v != 0) return set_error(OZ_ERR_TIMEOUT, "device-side wait timed out (code %d)", v);
   return OZ_OK;
 }
+
+extern "C" int64_t oz_launch_count(void) { return oz::g_launches.load(std::memory_order_relaxed); }

@@ -18,6 +18,9 @@ namespace oz {
 // ---------------------------------------------------------------------------
 int set_error(int code, const char *fmt, ...);
 int check_cuda(cudaError_t e, const char *what);
+// Kernel launches issued by the library (oz_launch_count), counted at each
+// launch site.
+void count_launch();
 
 // Device-side status word of this translation unit: kernels write a nonzero
 // code here when a bounded wait gives up.  Each .cu file exposes it through a
@@ -184,13 +187,6 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// Prefetch one 3-D TMA box into L2 (no shared memory, no completion signal).
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
-                   (uint64_t)map),
-               "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
-}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
 }
@@ -347,18 +343,6 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, ui
 }
 
 // 32 lanes x 32 bit, 16 consecutive columns per thread.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 // Wait for the warp's TMEM loads, with the destination registers passed
 // through the wait so that no use of them can be scheduled before it.
 __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {

@@ -504,6 +504,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, p), "cross_gemm_kernel launch");
 }
 

@@ -200,10 +200,6 @@ struct LevelP {
 constexpr float kMagicF = 12582912.0f;            // 1.5 * 2^23
 constexpr int kMagicFBits = 0x4B400000;
 
-// exact float(n) for |n| < 2^22
-__device__ __forceinline__ float small_int_to_float(int n) {
-  return __fsub_rn(__int_as_float(n + kMagicFBits), kMagicF);
-}
 // exact double(n) for any 32-bit n: 1.5 * 2^52 + n, minus 1.5 * 2^52
 __device__ __forceinline__ double int_to_double_exact(int n) {
   return __dsub_rn(__hiloint2double(0x43380000 + (n >> 31), n), 6755399441055744.0);
@@ -342,10 +338,6 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
           "r"(smem_u32(dst)),
       "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-__device__ __forceinline__ void tma_load_3d_plain(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                                  int c0, int c1, int c2) {
-  tma_load_3d(dst, map, bar, c0, c1, c2);
 }
 
 // Per-thread storage of one line's values and the level loop, shared by the
@@ -973,6 +965,7 @@ int launch_rows_nc(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lin
   const int64_t total = batch * (int64_t)lines;
   const int64_t groups = (total + (kRowCTA / T) - 1) / (kRowCTA / T);
   const int grid = (int)std::min<int64_t>(groups, (int64_t)sm_count_split());
+  count_launch();
   kern<<<grid, kRowCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
                                     reinterpret_cast<ST *>(slices), scales, NS, rowp);
   return check_cuda(cudaGetLastError(), "split_rows_tma launch");
@@ -1084,6 +1077,7 @@ int launch_cols_v(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int line
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   ST *o = reinterpret_cast<ST *>(slices);
+  count_launch();
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, map, lines, (int)batch, K, ld, s, alpha, o,
                                        scales, NS),
                     "split_cols_tma launch");
@@ -1128,6 +1122,7 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "cudaFuncSetAttribute(split_colpairs)"))
       return rc;
+    count_launch();
     kern<<<grid, kRowCTA, smem, st>>>(map, lines, panels, ppb, K, ld, s, alpha, o, scales, NS);
     *done = true;
     return check_cuda(cudaGetLastError(), "split_colpairs_tma launch");
@@ -1181,6 +1176,7 @@ int dispatch(const void *in_v, int64_t batch, int64_t lines, int64_t K, int64_t 
   if (rc != OZ_OK || done || try_only) return rc;
   using ST = typename SliceT<SK>::type;
   dim3 grid((unsigned)lines, (unsigned)batch);
+  count_launch();
   split_any_kernel<TIn, SK, EXACT><<<grid, kAnyThreads, 0, st>>>(
       in, sb, sl, sk, (int)lines, (int)K, (int)ld, s, alpha, reinterpret_cast<ST *>(slices), scales);
   return check_cuda(cudaGetLastError(), "split_any_kernel launch");
@@ -1237,6 +1233,7 @@ template <typename T>
 int transpose_into(const void *in, int64_t batch, int64_t lines, int64_t k, int64_t sb,
                    int64_t sk, int64_t kp, void *ws, cudaStream_t st) {
   dim3 grid((unsigned)((lines + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)batch);
+  count_launch();
   transpose_lines<T><<<grid, dim3(32, 8), 0, st>>>(reinterpret_cast<const T *>(in), sb, sk,
                                                    (int)lines, (int)k, (int)kp,
                                                    reinterpret_cast<T *>(ws));
@@ -1252,6 +1249,7 @@ int dispatch_int8_input(int slice_dtype, const void *in_v, int64_t batch, int64_
   const int8_t *in = reinterpret_cast<const int8_t *>(in_v);
   dim3 grid((unsigned)lines, (unsigned)batch);
 #define OZ_A(SK)                                                                             \
+  count_launch();                                                                             \
   split_any_kernel<int8_t, SK, false><<<grid, kAnyThreads, 0, st>>>(                          \
       in, sb, sl, sk, (int)lines, (int)K, (int)ld, s, alpha,                                  \
       reinterpret_cast<typename SliceT<SK>::type *>(slices), scales);                         \

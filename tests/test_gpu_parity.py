@@ -317,6 +317,19 @@ def test_split_fp64_column_pairs(sk, K, lines, s, residual):
     check_split(view, lines_np, s, alpha, sk, "fp64", residual=residual)
 
 
+def test_launch_count_of_a_matmul():
+    """oz_launch_count: an fp64 matmul is three library kernels (split of A's
+    rows, column-pair split of B, cross-GEMM) -- the count bench.py reports."""
+    from ozaki_triton_b200 import _lib
+    rng = np.random.default_rng(3)
+    a = to_dev(rng.standard_normal((512, 512)), "fp64")
+    b = to_dev(rng.standard_normal((512, 256)), "fp64")
+    lib = _lib.load()
+    n0 = lib.oz_launch_count()
+    oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.int8)
+    assert lib.oz_launch_count() - n0 == 3
+
+
 def test_int8_inputs_saturate_out_of_range():
     """int8 inputs (accepted by the reference) give an int8 C; results outside
     [-128, 127] saturate like the GPU's float-to-int8 conversion."""

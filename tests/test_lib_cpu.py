@@ -141,6 +141,15 @@ def test_blocked_gemm_and_peer_entries_validate_without_a_gpu():
     assert lib.oz_copy_async(p, p, 0, None) == _lib.OZ_OK
 
 
+def test_launch_count_is_not_moved_by_rejected_calls():
+    lib = _lib.load()
+    n0 = lib.oz_launch_count()
+    p = ctypes.c_void_p(256)
+    assert lib.oz_split(p, _lib.OZ_F64, 1, 4, 8, 32, 8, 1, 0, 7, _lib.OZ_I8, 0, p, 128, p,
+                        None) == _lib.OZ_ERR_INVALID
+    assert lib.oz_launch_count() == n0 >= 0
+
+
 def test_policy_tables_match_reference():
     # ozaki_triton.py:36-41, 62-73
     assert oz.SLICE_DTYPE_INFO[torch.float32] == (23, False)
