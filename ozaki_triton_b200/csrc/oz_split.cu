@@ -330,6 +330,38 @@ __device__ __forceinline__ typename QOut<SK>::type step_f32_rd(float &r, float i
   }
 }
 
+// Two int8 steps at once with the packed fp32 instructions of sm_100
+// (__fmul2/__fadd2/__ffma2: per component exactly the scalar operations
+// above, half the instructions).  EXACT_HALF / FMA_RESID select the fp64-
+// input (step_f32_exact) or fp32-input (step_f32_rd) arithmetic.
+template <bool BIG, bool EXACT_HALF>
+__device__ __forceinline__ void step2_i8(float &r0, float &r1, float inv2, float scale, bool upd,
+                                         uint32_t &w0, uint32_t &w1) {
+  float2 x = make_float2(r0, r1);
+  if constexpr (BIG) x = __fmul2_rn(x, make_float2(18446744073709551616.0f, 18446744073709551616.0f));
+  x = __fmul2_rn(x, make_float2(inv2, inv2));
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 t = EXACT_HALF ? __fadd2_rz(a, make_float2(0.5f, 0.5f))
+                              : __fadd2_rn(a, make_float2(0.5f, 0.5f));
+  const float2 f = __fadd2_rz(t, make_float2(kMagicF, kMagicF));
+  const float2 qa = __fadd2_rn(f, make_float2(-kMagicF, -kMagicF));   // floor(t), exact
+  const float2 q = make_float2(fminf(copysignf(qa.x, x.x), 127.0f),
+                               fminf(copysignf(qa.y, x.y), 127.0f));
+  const float2 m = __fadd2_rn(q, make_float2(kMagicF, kMagicF));
+  w0 = __float_as_uint(m.x);
+  w1 = __float_as_uint(m.y);
+  if (upd) {
+    float2 r = make_float2(r0, r1);
+    if constexpr (EXACT_HALF) {
+      r = __ffma2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale), r);   // exact
+    } else {
+      r = __fadd2_rn(r, __fmul2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale)));
+    }
+    r0 = r.x;
+    r1 = r.y;
+  }
+}
+
 // bulk (non-tensor) TMA copy global -> shared, completion counted on `bar`
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
                                           uint64_t *bar) {
@@ -391,6 +423,25 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
             if constexpr (EXACT) vd[i] = nd;
             else vf[i] = nf;
             emit(l, i, q);
+          }
+        }
+      } else if constexpr (SK == OZ_I8 && NV % 2 == 0) {
+        const float inv2 = lv.inv2();
+        if (!lv.big()) {
+#pragma unroll
+          for (int i = 0; i < NV; i += 2) {
+            uint32_t w0, w1;
+            step2_i8<false, F64IN>(vf[i], vf[i + 1], inv2, lv.scale, upd, w0, w1);
+            emit(l, i, w0);
+            emit(l, i + 1, w1);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < NV; i += 2) {
+            uint32_t w0, w1;
+            step2_i8<true, F64IN>(vf[i], vf[i + 1], inv2, lv.scale, upd, w0, w1);
+            emit(l, i, w0);
+            emit(l, i + 1, w1);
           }
         }
       } else if (!lv.big()) {
