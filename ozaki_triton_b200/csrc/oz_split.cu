@@ -335,9 +335,9 @@ __device__ __forceinline__ typename QOut<SK>::type step_f32_rd(float &r, float i
 // above, half the instructions).  EXACT_HALF / FMA_RESID select the fp64-
 // input (step_f32_exact) or fp32-input (step_f32_rd) arithmetic.
 template <bool BIG, bool EXACT_HALF>
-__device__ __forceinline__ void step2_i8(float &r0, float &r1, float inv2, float scale, bool upd,
+__device__ __forceinline__ void step2_i8(float2 &r, float inv2, float scale, bool upd,
                                          uint32_t &w0, uint32_t &w1) {
-  float2 x = make_float2(r0, r1);
+  float2 x = r;
   if constexpr (BIG) x = __fmul2_rn(x, make_float2(18446744073709551616.0f, 18446744073709551616.0f));
   x = __fmul2_rn(x, make_float2(inv2, inv2));
   const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
@@ -351,14 +351,11 @@ __device__ __forceinline__ void step2_i8(float &r0, float &r1, float inv2, float
   w0 = __float_as_uint(m.x);
   w1 = __float_as_uint(m.y);
   if (upd) {
-    float2 r = make_float2(r0, r1);
     if constexpr (EXACT_HALF) {
       r = __ffma2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale), r);   // exact
     } else {
       r = __fadd2_rn(r, __fmul2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale)));
     }
-    r0 = r.x;
-    r1 = r.y;
   }
 }
 
@@ -381,11 +378,13 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
   using QT = typename QOut<SK>::type;
   static constexpr bool F64IN = sizeof(TIn) == 8;
   double vd[F64IN ? NV : 1];
-  float vf[NV];
+  // fp32 values as register pairs (the packed f32x2 steps take both halves)
+  float2 vf2[(NV + 1) / 2];
+  __device__ __forceinline__ float &vf(int i) { return (i & 1) ? vf2[i >> 1].y : vf2[i >> 1].x; }
 
   __device__ __forceinline__ void set(int i, TIn v) {
     if constexpr (F64IN) vd[i] = v;
-    else vf[i] = InTraits<TIn>::to_float(v);
+    else vf(i) = InTraits<TIn>::to_float(v);
   }
 
   // emit(l, i, q) stores one slice element (q as QOut: see there) and must
@@ -406,7 +405,7 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
       } else {
         m = 0.f;
 #pragma unroll
-        for (int i = 0; i < NV; ++i) m = fmaxf(m, fabsf(vf[i]));
+        for (int i = 0; i < NV; ++i) m = fmaxf(m, fabsf(vf(i)));
       }
       m = reduce(m, l);
       LevelP lv;
@@ -421,7 +420,7 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
             float nf = 0.f;
             QT q = step_f64<SK, EXACT>(vd[i], inv_d, lv.scale, upd, nd, nf);
             if constexpr (EXACT) vd[i] = nd;
-            else vf[i] = nf;
+            else vf(i) = nf;
             emit(l, i, q);
           }
         }
@@ -431,7 +430,7 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
 #pragma unroll
           for (int i = 0; i < NV; i += 2) {
             uint32_t w0, w1;
-            step2_i8<false, F64IN>(vf[i], vf[i + 1], inv2, lv.scale, upd, w0, w1);
+            step2_i8<false, F64IN>(vf2[i >> 1], inv2, lv.scale, upd, w0, w1);
             emit(l, i, w0);
             emit(l, i + 1, w1);
           }
@@ -439,7 +438,7 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
 #pragma unroll
           for (int i = 0; i < NV; i += 2) {
             uint32_t w0, w1;
-            step2_i8<true, F64IN>(vf[i], vf[i + 1], inv2, lv.scale, upd, w0, w1);
+            step2_i8<true, F64IN>(vf2[i >> 1], inv2, lv.scale, upd, w0, w1);
             emit(l, i, w0);
             emit(l, i + 1, w1);
           }
@@ -449,8 +448,8 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           QT q;
-          if constexpr (F64IN) q = step_f32_exact<SK, false>(vf[i], inv2, lv.scale, upd);
-          else q = step_f32_rd<SK, false>(vf[i], inv2, lv.scale, upd);
+          if constexpr (F64IN) q = step_f32_exact<SK, false>(vf(i), inv2, lv.scale, upd);
+          else q = step_f32_rd<SK, false>(vf(i), inv2, lv.scale, upd);
           emit(l, i, q);
         }
       } else {
@@ -458,8 +457,8 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           QT q;
-          if constexpr (F64IN) q = step_f32_exact<SK, true>(vf[i], inv2, lv.scale, upd);
-          else q = step_f32_rd<SK, true>(vf[i], inv2, lv.scale, upd);
+          if constexpr (F64IN) q = step_f32_exact<SK, true>(vf(i), inv2, lv.scale, upd);
+          else q = step_f32_rd<SK, true>(vf(i), inv2, lv.scale, upd);
           emit(l, i, q);
         }
       }
