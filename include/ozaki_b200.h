@@ -213,6 +213,16 @@ int oz_device_status(void *stream, int32_t *code);
  * region: the difference of two readings). */
 int64_t oz_launch_count(void);
 
+/*
+ * Self-test of the device-side failure detection (no counterpart in the
+ * reference): one thread waits on a barrier that nothing arrives on, with
+ * the kernels' bounded wait cut to bound_cycles SM cycles (at most the
+ * kernels' own bound, ~2 s).  The wait gives up, the kernel returns normally
+ * and the next oz_device_status reports OZ_ERR_TIMEOUT with code 9.  No
+ * fault, no trap; the context stays usable.
+ */
+int oz_wait_selftest(int64_t bound_cycles, void *stream);
+
 /* Message for the last error returned on the calling thread ("" if none). */
 const char *oz_last_error(void);
 

@@ -47,6 +47,7 @@ SIGNATURES = {
     "oz_copy_async": (_int, [_vp, _vp, _i64, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),
     "oz_launch_count": (_i64, []),
+    "oz_wait_selftest": (_int, [_i64, _vp]),
     "oz_last_error": (ctypes.c_char_p, []),
     "oz_version": (ctypes.c_char_p, []),
 }

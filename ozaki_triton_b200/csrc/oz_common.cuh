@@ -53,6 +53,7 @@ enum DeviceCode : int {
   DEV_TIMEOUT_MMA = 2,
   DEV_TIMEOUT_EPILOGUE = 3,
   DEV_TIMEOUT_CLUSTER = 4,
+  DEV_TIMEOUT_SELFTEST = 9,   // oz_wait_selftest: a wait that nothing satisfies
 };
 
 // Upper bound for any spin-wait, in SM clock cycles (~2 s at 1.9 GHz).
@@ -161,7 +162,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // Bounded wait on an mbarrier phase.  Returns false (and raises *abort) when
 // the bound is hit or another role already aborted; never traps.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  volatile int *abort, int code) {
+                                                  volatile int *abort, int code,
+                                                  long long bound = kWaitBoundCycles) {
   uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   long long t0 = clock64();
@@ -169,7 +171,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 63u) == 63u) {
       if (*abort) return false;
-      if (clock64() - t0 > kWaitBoundCycles) {
+      if (clock64() - t0 > bound) {
         *abort = code;
         atomicCAS(&g_device_status, 0, code);
         return false;

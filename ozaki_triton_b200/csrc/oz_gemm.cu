@@ -662,6 +662,33 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
 }  // namespace
 }  // namespace oz
 
+namespace oz {
+namespace {
+// One thread waits on a shared-memory barrier that nothing arrives on, with
+// the same bounded wait the GEMM's roles use, for `bound` SM cycles: the wait
+// gives up, records DEV_TIMEOUT_SELFTEST in this unit's status word and the
+// kernel returns normally (no trap, the context stays usable).
+__global__ void wait_selftest_kernel(long long bound) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  abort_flag = 0;
+  (void)mbar_wait_bounded(&bar, 0, &abort_flag, DEV_TIMEOUT_SELFTEST, bound);
+}
+}  // namespace
+}  // namespace oz
+
+extern "C" int oz_wait_selftest(int64_t bound_cycles, void *stream) {
+  using namespace oz;
+  if (bound_cycles <= 0 || bound_cycles > kWaitBoundCycles)
+    return set_error(OZ_ERR_INVALID, "bound must be in (0, %lld] cycles", kWaitBoundCycles);
+  count_launch();
+  wait_selftest_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      (long long)bound_cycles);
+  return check_cuda(cudaGetLastError(), "wait_selftest_kernel launch");
+}
+
 extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_scales,
                              const float *b_scales, int64_t batch, int64_t m, int64_t n,
                              int64_t k, int64_t ld, int32_t num_splits, int slice_dtype,

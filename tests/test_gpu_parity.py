@@ -317,6 +317,28 @@ def test_split_fp64_column_pairs(sk, K, lines, s, residual):
     check_split(view, lines_np, s, alpha, sk, "fp64", residual=residual)
 
 
+def test_bounded_wait_times_out_and_the_context_stays_usable():
+    """Failure detection without a GPU fault: a kernel waits on a barrier that
+    nothing arrives on, gives up after a short bound (~0.1 s of SM cycles),
+    records its code and returns; the host reads the timeout, and the next
+    computation on the same context is correct."""
+    from ozaki_triton_b200 import _lib
+    lib = _lib.load()
+    assert oz.device_status() == 0
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.oz_wait_selftest(200_000_000, st))
+    with pytest.raises(_lib.OzakiError) as ei:
+        oz.device_status()
+    assert ei.value.status == _lib.OZ_ERR_TIMEOUT and "code 9" in str(ei.value)
+    assert oz.device_status() == 0                      # the code was cleared by the read
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((200, 96)); b = rng.standard_normal((96, 72))
+    c = oz.ozaki_matmul(to_dev(a, "fp64"), to_dev(b, "fp64"), num_splits=3,
+                        slice_dtype=torch.int8)
+    assert same_bits(host(c), oracle.ozaki_matmul(a, b, 3, "int8", "fp64"))
+    assert lib.oz_wait_selftest(0, st) == _lib.OZ_ERR_INVALID
+
+
 def test_launch_count_of_a_matmul():
     """oz_launch_count: an fp64 matmul is three library kernels (split of A's
     rows, column-pair split of B, cross-GEMM) -- the count bench.py reports."""

@@ -141,6 +141,12 @@ def test_blocked_gemm_and_peer_entries_validate_without_a_gpu():
     assert lib.oz_copy_async(p, p, 0, None) == _lib.OZ_OK
 
 
+def test_wait_selftest_validates_its_bound_without_a_gpu():
+    lib = _lib.load()
+    assert lib.oz_wait_selftest(0, None) == _lib.OZ_ERR_INVALID
+    assert lib.oz_wait_selftest(10 ** 12, None) == _lib.OZ_ERR_INVALID
+
+
 def test_launch_count_is_not_moved_by_rejected_calls():
     lib = _lib.load()
     n0 = lib.oz_launch_count()
