@@ -299,6 +299,8 @@ class PeerBlocks:
                                  sc[0, q].data_ptr(), self.peer[(q, 2 + par)][0] + q * bsc, bsc)
             self.blocks.append((views, copies))
         self.ready = torch.cuda.Event()
+        self.b_split = torch.cuda.Event()
+        self.bar_stream = torch.cuda.Stream(dev)
         self.a_ready = torch.cuda.Event()
         self.arrived = [torch.cuda.Event() for _ in range(self.world)]
 
@@ -379,9 +381,14 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
                  sc[0, rank])
     # every rank's panel is split, and no peer still copies from the buffer
     # set this call reuses (its copies of two calls ago ended before it
-    # entered this all-reduce)
-    dist.all_reduce(pb.flag, group=group)
-    pb.ready.record(cur)
+    # entered this all-reduce).  The all-reduce runs on a stream of its own
+    # that waits for the panel's split only, so the split of A's rows and the
+    # GEMM of the own block go ahead on the current stream meanwhile.
+    pb.b_split.record(cur)
+    pb.bar_stream.wait_event(pb.b_split)
+    with torch.cuda.stream(pb.bar_stream):
+        dist.all_reduce(pb.flag, group=group)
+        pb.ready.record(pb.bar_stream)
     A3 = A_local.reshape(1, m_loc, k)
     a_sl, a_sc = backend.split(A3, A3.stride(1), A3.stride(2), m_loc, k, num_splits, alpha,
                                slice_dtype, mode)
@@ -420,6 +427,7 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
     # streams still read or write them
     for gs in gemm_streams:
         cur.wait_stream(gs)
+    cur.wait_event(pb.ready)             # the barrier is part of the call
     return c
 
 
