@@ -73,7 +73,11 @@ int64_t oz_slice_row_bytes(int64_t k, int slice_dtype);
  *   in        : element (b, line, k) at in + b*stride_b + line*stride_line + k*stride_k
  *               (element strides).  Lines are the rows of A, or the columns of B
  *               (B is split through its transposed view, ozaki_triton.py:593).
- *               Supported layouts: stride_k == 1, or stride_line == 1.
+ *               Any strides.  Fast kernels: stride_k == 1 (rows); stride_line ==
+ *               1 (columns) through a column kernel where one applies (fp64:
+ *               pairs of columns from 2-D TMA boxes, K <= 8192, 16-byte row
+ *               pitch; fp32/fp16/bf16: a cluster kernel); other layouts and
+ *               int8 inputs take a generic kernel.
  *   slices    : (batch, num_splits, lines, ld) of slice_dtype, ld = row pitch in
  *               elements (oz_slice_row_bytes(k)/elem_size); k-contiguous.
  *   scales    : (batch, num_splits, lines) fp32 powers of two.
@@ -87,9 +91,9 @@ int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t
 /*
  * Scratch bytes that oz_split_ex can use for this input layout (0 when none
  * helps).  When the lines are contiguous (stride_line == 1: the columns of a
- * row-major B) oz_split_ex first transposes them into the workspace
- * ((batch, lines, k padded to 16 bytes), input dtype) so that each line is
- * read as one contiguous row by the row kernel.
+ * row-major B) and no column kernel applies, oz_split_ex transposes them into
+ * the workspace ((batch, lines, k padded to 16 bytes), input dtype) so that
+ * each line is read as one contiguous row by the row kernel.
  */
 int64_t oz_split_workspace_bytes(int in_dtype, int64_t batch, int64_t lines, int64_t k,
                                  int64_t stride_line, int64_t stride_k);
@@ -97,8 +101,8 @@ int64_t oz_split_workspace_bytes(int in_dtype, int64_t batch, int64_t lines, int
 /*
  * oz_split with caller-provided scratch memory (device, 16-byte aligned).
  * Same results as oz_split; with workspace_bytes >= oz_split_workspace_bytes()
- * the column layout goes through the transpose described above, otherwise
- * it behaves exactly like oz_split.  Also replaces split_matrix
+ * a column layout that no column kernel takes goes through the transpose
+ * described above, otherwise it behaves exactly like oz_split.  Also replaces split_matrix
  * (ozaki_triton.py:214-256), whose fp32 residual buffer is a workspace too.
  */
 int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,

@@ -1,4 +1,4 @@
-// oz_split.cu -- single-pass split of FP64/FP32/FP16/BF16 lines into
+// oz_split.cu -- single-pass split of FP64/FP32/FP16/BF16/INT8 lines into
 // num_splits low-precision slices plus power-of-two scales (sm_100a).
 //
 // Replaces split_matrix_kernel (ozaki_triton.py:136-211) and its wrapper
@@ -17,19 +17,24 @@
 // Division by the power of two is done as an exact multiplication by its
 // reciprocal (same correctly rounded result).
 //
-// Three kernels:
-//   split_rows_kernel : the split axis is contiguous (rows of A).  A group of
-//                       T threads owns a line; coalesced 16-byte loads.
-//   split_cols_kernel : the lines are contiguous (columns of B, split through
-//                       B's transposed view like ozaki_triton.py:593).  A
-//                       cluster of up to 8 CTAs shares one panel of W columns
-//                       along K; per-level column maxima are combined through
-//                       distributed shared memory; slices are transposed in
-//                       shared memory and written K-contiguous.
-//   split_any_kernel  : any strides / any K.  Recomputes the residual chain
-//                       from the input on each level instead of holding it
-//                       (s + 1 reads of the line); used only when the two
-//                       fast kernels do not apply.
+// Kernels:
+//   split_rows_tma     : the split axis is contiguous (rows of A, or rows of a
+//                        transposed workspace).  512 threads own a line;
+//                        whole lines arrive by bulk TMA copies.
+//   split_colpairs_tma : fp64 lines that are contiguous columns of a row-major
+//                        B (split through B's transposed view like
+//                        ozaki_triton.py:593), two per iteration, from 2-D TMA
+//                        boxes; no transposed copy.
+//   split_cols_tma     : contiguous columns of other dtypes: a cluster of up
+//                        to 8 CTAs shares one panel of W columns along K;
+//                        per-level column maxima are combined through
+//                        distributed shared memory; slices are transposed in
+//                        shared memory and written K-contiguous.
+//   transpose_lines    : columns into a K-contiguous workspace where neither
+//                        column kernel applies (then split_rows_tma).
+//   split_any_kernel   : any strides / any K, and int8 inputs.  Recomputes
+//                        the residual chain from the input on each level
+//                        instead of holding it (s + 1 reads of the line).
 
 #include <algorithm>
 #include <cstdio>
