@@ -196,6 +196,33 @@ def test_sharded_two_ranks_bit_identical(tmp_path):
         assert np.array_equal(got, oracle.ozaki_matmul(A.numpy(), B.numpy(), 4, "int8", "fp64"))
 
 
+def case_world3(rank, world, out_dir):
+    """Three ranks: ragged panels (256, 256, 88 columns), uneven rows, and the
+    root broadcast in two blocks."""
+    g = torch.Generator().manual_seed(9)
+    A = law(g, (37, 64))
+    B = law(g, (64, 600))
+    lo, hi = ozd.block_range(37, world, rank)
+    c0, c1 = ozd.column_panel(600, world, rank)
+    c = ozd.ozaki_matmul_sharded(A[lo:hi], B[:, c0:c1], 3, torch.int8, backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"s{rank}.npy"), c.numpy())
+    d = ozd.ozaki_matmul_mrows(A[lo:hi], B if rank == 1 else None, 3, torch.int8, root=1,
+                               b_blocks=2, backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"m{rank}.npy"), d.numpy())
+
+
+def test_three_ranks_sharded_and_root_broadcast(tmp_path):
+    codes = run_ranks(case_world3, 3, tmp_path)
+    assert codes == [0, 0, 0], [open(p).read() for p in tmp_path.glob("err*.txt")]
+    g = torch.Generator().manual_seed(9)
+    A = law(g, (37, 64))
+    B = law(g, (64, 600))
+    want = oracle.ozaki_matmul(A.numpy(), B.numpy(), 3, "int8", "fp64")
+    for tag in ("s", "m"):
+        got = np.concatenate([np.load(tmp_path / f"{tag}{r}.npy") for r in range(3)])
+        assert np.array_equal(got, want), tag
+
+
 def test_column_panels_cover_n():
     for n in [0, 1, 100, 128, 129, 600, 8192, 8193]:
         for world in [1, 2, 3, 8]:
