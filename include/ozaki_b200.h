@@ -124,7 +124,8 @@ int oz_split_ex(const void *in, int in_dtype, int64_t batch, int64_t lines, int6
  * from a fixed array of oz_split_noalloc_max_bytes() bytes (32 MiB) that the
  * library keeps in device memory of every GPU it is loaded on, until the
  * process exits.  Inputs needing more scratch are rejected with
- * OZ_ERR_INVALID before any launch.  The first call on a device looks up the
+ * OZ_ERR_INVALID before any launch, unless a column kernel takes them
+ * without scratch (fp64 column pairs, or the cluster kernel).  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before
  * any stream capture.  All calls share the one array: calls that overlap on
  * the GPU (different streams, or different host threads on one device) race

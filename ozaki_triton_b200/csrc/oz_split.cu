@@ -1319,10 +1319,13 @@ int dispatch_int8_input(int slice_dtype, const void *in_v, int64_t batch, int64_
   return check_cuda(cudaGetLastError(), "split_any_kernel launch");
 }
 
+// fast_only != nullptr: launch only a row or column kernel and report in
+// *fast_only whether one applied (never the generic kernel).
 int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,
                int64_t stride_b, int64_t stride_line, int64_t stride_k, int32_t num_splits,
                int32_t alpha, int slice_dtype, int residual_mode, void *slices, int64_t ld,
-               float *scales, void *workspace, int64_t workspace_bytes, void *stream) {
+               float *scales, void *workspace, int64_t workspace_bytes, void *stream,
+               bool *fast_only = nullptr) {
   if (num_splits < 1 || num_splits > kMaxSplits)
     return set_error(OZ_ERR_INVALID, "num_splits must be in [1, %d], got %d", kMaxSplits,
                      num_splits);
@@ -1421,21 +1424,28 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
   }
   switch (in_dtype) {
     case OZ_I8:
+      if (fast_only) {
+        *fast_only = false;
+        return OZ_OK;
+      }
       return dispatch_int8_input(slice_dtype, in, batch, lines, k, stride_b, stride_line,
                                  stride_k, num_splits, alpha, slices, ld, scales, st);
     case OZ_F64:
       return dispatch_slice<double>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
-                                    stride_line, stride_k, num_splits, alpha, slices, ld, scales, st);
+                                    stride_line, stride_k, num_splits, alpha, slices, ld, scales,
+                                    st, fast_only);
     case OZ_F32:
       return dispatch_slice<float>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
-                                   stride_line, stride_k, num_splits, alpha, slices, ld, scales, st);
+                                   stride_line, stride_k, num_splits, alpha, slices, ld, scales,
+                                   st, fast_only);
     case OZ_F16:
       return dispatch_slice<__half>(slice_dtype, residual_mode, in, batch, lines, k, stride_b,
-                                    stride_line, stride_k, num_splits, alpha, slices, ld, scales, st);
+                                    stride_line, stride_k, num_splits, alpha, slices, ld, scales,
+                                    st, fast_only);
     default:
       return dispatch_slice<__nv_bfloat16>(slice_dtype, residual_mode, in, batch, lines, k,
                                            stride_b, stride_line, stride_k, num_splits, alpha,
-                                           slices, ld, scales, st);
+                                           slices, ld, scales, st, fast_only);
   }
 }
 
@@ -1516,11 +1526,20 @@ extern "C" int oz_split_noalloc(const void *in, int in_dtype, int64_t batch, int
   using namespace oz;
   const int64_t need =
       oz_split_workspace_bytes(in_dtype, batch, lines, k, stride_line, stride_k);
-  if (need > kNoAllocScratchBytes)
+  if (need > kNoAllocScratchBytes) {
+    // a column kernel that needs no scratch (fp64 column pairs, the cluster
+    // kernel) still takes it; otherwise the input is rejected
+    bool fast = false;
+    if (int rc = split_impl(in, in_dtype, batch, lines, k, stride_b, stride_line, stride_k,
+                            num_splits, alpha, slice_dtype, residual_mode, slices, ld, scales,
+                            nullptr, 0, stream, &fast))
+      return rc;
+    if (fast) return OZ_OK;
     return set_error(OZ_ERR_INVALID,
                      "oz_split_noalloc: this input needs %lld bytes of scratch, more than the "
                      "library's fixed %lld-byte device array; use oz_split_ex with a workspace",
                      (long long)need, (long long)kNoAllocScratchBytes);
+  }
   void *scratch = nullptr;
   if (need > 0)
     if (int rc = scratch_address(&scratch)) return rc;

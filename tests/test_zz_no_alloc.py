@@ -65,3 +65,34 @@ def test_noalloc_rejects_inputs_beyond_the_scratch():
                               p, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.OZ_ERR_INVALID
     assert "scratch" in lib.oz_last_error().decode()
+
+
+def test_noalloc_takes_large_fp64_columns_without_scratch():
+    """fp64 columns whose transposed copy would exceed the array, but which the
+    column-pair kernel splits without scratch, are accepted; same bits as
+    oz_split_ex."""
+    from ozaki_triton_b200 import _lib
+    lib = _lib.load()
+    K, N, s = 4096, 2048, 4
+    assert lib.oz_split_workspace_bytes(_lib.OZ_F64, 1, N, K, 1, N) > lib.oz_split_noalloc_max_bytes()
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(1, K, N, generator=g, dtype=torch.float64, device=DEV)
+    alpha = 7
+    ld = K
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for noalloc in (True, False):
+        sl = torch.full((1, s, N, ld), 77, dtype=torch.int8, device=DEV)
+        sc = torch.full((1, s, N), -1.0, dtype=torch.float32, device=DEV)
+        args = [x.data_ptr(), _lib.OZ_F64, 1, N, K, K * N, 1, N, s, alpha, _lib.OZ_I8, 0,
+                sl.data_ptr(), ld, sc.data_ptr()]
+        if noalloc:
+            _lib.check(lib.oz_split_noalloc(*args, st))
+        else:
+            need = lib.oz_split_workspace_bytes(_lib.OZ_F64, 1, N, K, 1, N)
+            ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+            _lib.check(lib.oz_split_ex(*args, ws.data_ptr(), need, st))
+        torch.cuda.synchronize()
+        outs.append((sl, sc))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
