@@ -125,7 +125,16 @@ def main(ref_dir: str):
         ("rows_i8_i8_s2", "int8", "int8", 2, 1, 12, 96, "rows"),
         ("rows_i8_f32_s1", "int8", "fp32", 1, 1, 8, 64, "rows"),
         ("cols_i8_f16_s3", "int8", "fp16", 3, 1, 24, 80, "cols"),
+        # more shapes and types, from their own generator as well
+        ("rows_bf16_i8_s3", "bf16", "int8", 3, 1, 12, 200, "rows"),
+        ("cols_f32_i8_s4", "fp32", "int8", 4, 1, 30, 300, "cols"),
+        ("rows_f64_i8_s4_k8192", "fp64", "int8", 4, 1, 10, 8192, "rows"),
+        ("cols_f64_i8_s2_k4100", "fp64", "int8", 2, 1, 12, 4100, "cols"),
+        ("cols_f16_f16_s2", "fp16", "fp16", 2, 1, 16, 130, "cols"),
     ]
+    extra_split = {"rows_bf16_i8_s3", "cols_f32_i8_s4", "rows_f64_i8_s4_k8192",
+                   "cols_f64_i8_s2_k4100", "cols_f16_f16_s2"}
+    rng_x = np.random.default_rng(9)
     rng_i8 = np.random.default_rng(8)
     for name, ik, sk, s, B, L, K, layout in split_cases:
         if ik == "int8":
@@ -134,8 +143,9 @@ def main(ref_dir: str):
             x[0, 3] = 0; x[0, 3, K // 2] = 5                     # single nonzero
             x[0, 4] = np.where(np.arange(K) % 2 == 0, 1, -1)     # alternating signs
         else:
-            x = spread(rng, (B, L, K))
-            sp = special_rows(rng, K, ik)
+            r = rng_x if name in extra_split else rng
+            x = spread(r, (B, L, K))
+            sp = special_rows(r, K, ik)
             assert np.all(np.isfinite(torch.from_numpy(sp).to(tdt[ik]).double().numpy()))
             n_sp = min(len(sp), L)
             x[0, :n_sp] = sp[:n_sp]
@@ -181,11 +191,19 @@ def main(ref_dir: str):
         # depends on the backend)
         ("mm_i8_i8_s2", "int8", "int8", 2, (24, 8), (8, 16), "int_small"),
         ("mm_i8_f16_s1", "int8", "fp16", 1, (12, 6), (6, 10), "int_small"),
+        # more shapes and types (own generator; no bf16 C: the interpreter's
+        # float-to-bf16 conversion truncates, unlike the GPU's)
+        ("mm_f64_i8_s4_k2048", "fp64", "int8", 4, (64, 2048), (2048, 32), "c3_x"),
+        ("mm_f32_i8_s3_bcast", "fp32", "int8", 3, (2, 3, 16, 40), (3, 40, 8), "normal_x"),
     ]
     for name, ik, sk, s, ash, bsh, law in mm_cases:
         if law == "int_small":
             a = rng_i8.integers(-3, 4, ash).astype(np.float64)
             b = rng_i8.integers(-3, 4, bsh).astype(np.float64)
+        elif law == "normal_x":
+            a = rng_x.standard_normal(ash); b = rng_x.standard_normal(bsh)
+        elif law == "c3_x":
+            a = c3_dist(rng_x, ash); b = c3_dist(rng_x, bsh)
         elif law == "c3":
             a = c3_dist(rng, ash); b = c3_dist(rng, bsh)
         elif law == "spread":
