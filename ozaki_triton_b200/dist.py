@@ -434,7 +434,7 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
 def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_splits: int = 3,
                          slice_dtype: torch.dtype = torch.float16, *, n: Optional[int] = None,
                          group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
-                         transport: str = "collective",
+                         transport: str = "auto",
                          backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B with A sharded by rows and B by column panels.
 
@@ -448,6 +448,8 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
     of the single-GPU ``ozaki_matmul``.
 
     ``transport``:
+    * ``"auto"`` (default): ``"p2p"`` for CUDA tensors in an NCCL group, else
+      ``"collective"``;
     * ``"collective"``: one all-gather (NCCL, or gloo on CPU) while the A rows
       are split, then one GEMM over all of N;
     * ``"p2p"`` (NCCL groups of one process per GPU): every rank maps its
@@ -461,7 +463,10 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
     dev = A_local.device
     _check_args(A_local.dtype, num_splits, slice_dtype)
     assert A_local.dtype == B_local.dtype
-    assert transport in ("collective", "p2p"), f"unknown transport {transport!r}"
+    assert transport in ("auto", "collective", "p2p"), f"unknown transport {transport!r}"
+    if transport == "auto":
+        transport = ("p2p" if A_local.is_cuda and dist.get_backend(group) == "nccl"
+                     else "collective")
     m_loc, k = A_local.shape
     assert B_local.shape[0] == k, f"contraction dim mismatch: {A_local.shape} @ {B_local.shape}"
     rank = dist.get_rank(group)
