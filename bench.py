@@ -470,8 +470,7 @@ def run_single(args):
 
         def e2e_step():
             # the public host-operand call: copies pipelined with the splits/GEMMs
-            oz.ozaki_matmul_from_host(a_pin, b_pin, num_splits=s, slice_dtype=sd,
-                                      out=c_pin if a_pin.dim() == 2 else None)
+            oz.ozaki_matmul_from_host(a_pin, b_pin, num_splits=s, slice_dtype=sd, out=c_pin)
 
         for _ in range(2):
             e2e_step()
