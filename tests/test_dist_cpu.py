@@ -158,6 +158,35 @@ def case_root_fails(rank, world, out_dir):
         fh.write("NO ERROR")
 
 
+def case_panel_rank_fails(rank, world, out_dir):
+    """A non-root rank dies before the all-gather of the sharded path: the
+    surviving rank's collective must end with an error, not hang."""
+    g = torch.Generator().manual_seed(10)
+    A = law(g, (8, 16))
+    B = law(g, (16, 300))
+    c0, c1 = ozd.column_panel(300, world, rank)
+    if rank == 1:
+        raise RuntimeError("injected failure before the all-gather")
+    t0 = time.time()
+    try:
+        ozd.ozaki_matmul_sharded(A, B[:, c0:c1], 2, torch.int8, n=300, backend=OracleBackend())
+    except Exception as e:  # noqa: BLE001
+        with open(os.path.join(out_dir, "peer_error.txt"), "w") as fh:
+            fh.write(f"{type(e).__name__} after {time.time() - t0:.1f}s: {e}")
+        return
+    with open(os.path.join(out_dir, "peer_error.txt"), "w") as fh:
+        fh.write("NO ERROR")
+
+
+def test_panel_rank_failure_is_reported_not_hung(tmp_path):
+    t0 = time.time()
+    codes = run_ranks(case_panel_rank_fails, 2, tmp_path)
+    assert codes[1] != 0                       # the injected failure
+    msg = (tmp_path / "peer_error.txt").read_text()
+    assert msg != "NO ERROR", msg              # the survivor saw an error ...
+    assert time.time() - t0 < 110              # ... within the timeout, no hang
+
+
 def test_block_range_covers_everything():
     for total in [0, 1, 7, 128, 8192, 8193]:
         for world in [1, 2, 3, 4, 8]:
