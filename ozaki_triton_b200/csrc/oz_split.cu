@@ -532,8 +532,8 @@ __device__ __forceinline__ void store_slices(typename SliceT<SK>::type *dst,
 // holds elements [(c*T + tl)*VEC, +VEC) for c < NCH (16- or 32-byte chunks:
 // the shared-memory reads are conflict-free or 2-way, the slice stores
 // coalesce).
-template <typename TIn, int SK, int T, int NCH, bool EXACT>
-__global__ void __launch_bounds__(kRowCTA, 1)
+template <typename TIn, int SK, int T, int NCH, bool EXACT, int CTA = kRowCTA>
+__global__ void __launch_bounds__(CTA, kRowCTA / CTA)
     split_rows_tma(const TIn *__restrict__ in, int64_t stride_b, int64_t stride_line, int lines,
                    int64_t total, int K, int ld, int s, int alpha,
                    typename SliceT<SK>::type *__restrict__ out, float *__restrict__ scales, int NS,
@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(kRowCTA, 1)
   using QT = typename QOut<SK>::type;
   constexpr int VEC = row_vec<TIn>();
   constexpr int NV = NCH * VEC;
-  constexpr int RPS = kRowCTA / T;
+  constexpr int RPS = CTA / T;
   extern __shared__ __align__(128) unsigned char smem[];
   const int stage = RPS * rowp;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + NS * stage);
@@ -1006,23 +1006,24 @@ int sm_count_split() {
   return n;
 }
 
-template <typename TIn, int SK, bool EXACT, int T, int NC>
+template <typename TIn, int SK, bool EXACT, int T, int NC, int CTA = kRowCTA>
 int launch_rows_nc(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K, int ld,
                    int s, int alpha, void *slices, float *scales, cudaStream_t st, int NS,
                    int rowp) {
   using ST = typename SliceT<SK>::type;
-  auto kern = split_rows_tma<TIn, SK, T, NC, EXACT>;
-  const int smem = NS * (kRowCTA / T) * rowp + kRowMaxStages * 8 + 2 * 16 * 4;
+  auto kern = split_rows_tma<TIn, SK, T, NC, EXACT, CTA>;
+  const int smem = NS * (CTA / T) * rowp + kRowMaxStages * 8 + 2 * 16 * 4;
   if (int rc = check_cuda(
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
           "cudaFuncSetAttribute(split_rows)"))
     return rc;
   const int64_t total = batch * (int64_t)lines;
-  const int64_t groups = (total + (kRowCTA / T) - 1) / (kRowCTA / T);
-  const int grid = (int)std::min<int64_t>(groups, (int64_t)sm_count_split());
+  const int64_t groups = (total + (CTA / T) - 1) / (CTA / T);
+  const int grid =
+      (int)std::min<int64_t>(groups, (int64_t)sm_count_split() * (kRowCTA / CTA));
   count_launch();
-  kern<<<grid, kRowCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
-                                    reinterpret_cast<ST *>(slices), scales, NS, rowp);
+  kern<<<grid, CTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
+                                reinterpret_cast<ST *>(slices), scales, NS, rowp);
   return check_cuda(cudaGetLastError(), "split_rows_tma launch");
 }
 
@@ -1059,6 +1060,24 @@ int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines,
   if (c64 <= 4) return go(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
   if (c512 <= 1) return go(std::integral_constant<int, 512>{}, std::integral_constant<int, 1>{});
   if (c512 <= 2) return go(std::integral_constant<int, 512>{}, std::integral_constant<int, 2>{});
+  if constexpr (sizeof(TIn) == 8) {
+    // fp64 rows of up to 8192 elements: two 256-thread CTAs per SM, one row
+    // each -- two independent barrier domains per SM instead of one (0.228
+    // vs 0.264 ms for 8192^2 with 4 int8 slices).  OZ_SPLIT_ROWS_CTA=512
+    // selects the single 512-thread CTA (benchmarking only).
+    static const bool two = [] {
+      const char *e = getenv("OZ_SPLIT_ROWS_CTA");
+      return !(e && atoi(e) == 512);
+    }();
+    if (two && c512 <= 4) {
+      const int NS = std::min(kRowMaxStages, (kRowSmem / 2) / rowp);
+      if (NS >= 1) {
+        *done = true;
+        return launch_rows_nc<TIn, SK, EXACT, 256, 8, 256>(in, sb, sl, batch, lines, K, ld, s,
+                                                          alpha, slices, scales, st, NS, rowp);
+      }
+    }
+  }
   if (c512 <= 4 && NC_MAX >= 4)
     return go(std::integral_constant<int, 512>{}, std::integral_constant<int, (NC_MAX >= 4 ? 4 : 2)>{});
   if (c512 <= 8 && NC_MAX >= 8)
