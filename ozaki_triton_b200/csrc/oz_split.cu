@@ -203,7 +203,6 @@ struct LevelP {
 };
 
 constexpr float kMagicF = 12582912.0f;            // 1.5 * 2^23
-constexpr int kMagicFBits = 0x4B400000;
 
 // exact double(n) for any 32-bit n: 1.5 * 2^52 + n, minus 1.5 * 2^52
 __device__ __forceinline__ double int_to_double_exact(int n) {
