@@ -3,24 +3,32 @@
 Workload (BASELINE.json headline, config "C3"): FP64 -> INT8 slices,
 num_splits = 4, one GEMM with M = N = K = 8192, entries
 x = (U(0,1) - 0.5) * exp(N(0,1)) from seed 2 (synthetic, generated on the
-host).  One step = one ``ozaki_matmul``: split of A by rows, split of B by
-columns, fused cross-GEMM over the 16 slice pairs with the FP64 epilogue.
+host).  One step = one public ``ozaki_matmul`` call: split of B by columns,
+split of A by rows, fused cross-GEMM over the 16 slice pairs with the FP64
+epilogue (``--config`` picks the other BASELINE.json configurations).
 
 * ``value``: emulated TFLOPS = 2*M*N*K / step time, inputs resident in HBM
   (A and B are 512 MiB each, larger than L2, so no flush is needed).
-* ``e2e``: the same metric through the public ``ozaki_matmul`` call with the
+* ``e2e``: the same metric through ``ozaki_matmul_from_host`` with the
   operands in pinned host memory: host->device copies of A and B and the
   device->host copy of C are inside the timed region.
-* ``roofline``: the cross-GEMM kernel, int8 tensor ops (pairs * 2MNK) per
-  launch over its CUDA-event duration, against 2x the measured dense bf16
-  peak (B200's dense int8 rate is twice its bf16 rate).
-* ``cpu_baseline``: the CPU restatement of the reference (oracle/) on a
-  bounded sample of the same workload, all host cores.
+* ``roofline``: the cross-GEMM kernel (CUDA events around its launch inside
+  the timed steps, ``oz_profile_next_gemm``), int8 tensor ops (pairs * 2MNK)
+  per launch over its duration, against the larger of 2x the measured dense
+  bf16 peak and the int8 rate cuBLAS reaches on this GPU (``torch._int_mm``
+  at 8192^3, measured in the same run).
+* comparators in the same run: cuBLAS DGEMM / SGEMM of the input dtype, CPU
+  ``torch.matmul`` in the input dtype on all host cores, and
+  ``cpu_baseline`` = the CPU restatement of the reference (oracle/) on a
+  bounded sample of the same workload.
 
-Multi-GPU (torchrun, N > 1): A is sharded by M rows, B lives on rank 0,
-which splits it once and broadcasts the int8 slices + scales over NCCL
-(``ozaki_triton_b200.dist``); every rank computes its C rows.  Total work is
-fixed, so scaling is "strong".  ``--impl reference`` times the reference
+Multi-GPU (torchrun, N > 1): ``bench_dist.py``.  By default A is sharded by
+rows and B by column panels; every rank splits its own panel and the panels'
+int8 slices are pulled from the peers over NVLink by copy engines
+(``--transport p2p``), each block's GEMM starting on arrival.  The same run
+also times the NCCL-broadcast layout (B on rank 0) and the gather of C to
+rank 0, and checks a sample of C bit for bit against the oracle.  Total work
+is fixed, so scaling is "strong".  ``--impl reference`` times the reference
 algorithm's CPU restatement on the host cores (rank 0 only).
 """
 
@@ -290,8 +298,8 @@ def main():
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1 or args.gpus > 1:
-        from ozaki_triton_b200 import dist_bench
-        dist_bench.main(args)
+        import bench_dist
+        bench_dist.main(args)
         return
     run_single(args)
 
@@ -338,12 +346,64 @@ def config_inputs(cfg):
     return a.to(cfg["dtype"]), b.to(cfg["dtype"])
 
 
+def int8_tensor_rate(dev, n: int = 8192, reps: int = 10) -> float:
+    """Dense int8 tensor rate cuBLAS reaches on this GPU (TOPS): torch._int_mm
+    at n^3 (int8 x int8 -> int32), best of ``reps`` launches timed with CUDA
+    events."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    bt = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    b = bt.t()                      # column-major B: the layout cuBLASLt takes natively
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    st = torch.cuda.current_stream(dev)
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        torch._int_mm(a, b)
+        e1.record(st)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def cpu_native_matmul(a_h: torch.Tensor, b_h: torch.Tensor, budget_flops: float = 2.3e12):
+    """CPU torch.matmul in the input dtype on all host cores: the whole
+    product when it is at most ``budget_flops``, else a block of A's rows
+    (full K and N) scaled to that budget."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    m, k = a_h.shape[-2:]
+    n = b_h.shape[-1]
+    bn = a_h.numel() // (m * k) if a_h.dim() > 2 else 1
+    bn = max(bn, b_h.numel() // (k * n) if b_h.dim() > 2 else 1)
+    full = 2.0 * bn * m * n * k
+    if full <= budget_flops:
+        a_s, b_s, sample = a_h, b_h, "the whole product"
+        flops = full
+    else:
+        a2 = a_h.reshape(-1, m, k)[0]
+        b2 = b_h.reshape(-1, k, n)[0]
+        rows = max(64, int(m * budget_flops / (2.0 * m * n * k)))
+        a_s, b_s = a2[:rows].contiguous(), b2
+        flops = 2.0 * rows * n * k
+        sample = f"{rows} rows of A (x full B) of one batch member"
+    torch.matmul(a_s[..., :64, :], b_s)              # warm-up (threads, kernels)
+    t0 = time.perf_counter()
+    torch.matmul(a_s, b_s)
+    dt = time.perf_counter() - t0
+    return {"value": flops / dt / 1e12, "unit": "TFLOPS", "cores": threads,
+            "dtype": str(a_h.dtype).replace("torch.", ""), "sample": sample,
+            "seconds": dt}
+
+
 def run_single(args):
     import math
 
     import ozaki_triton_b200 as oz
     from ozaki_triton_b200 import _lib
-    from ozaki_triton_b200.api import _OZ_DTYPE, _batch_index, _split_lines
 
     name = args.config
     cfg = CONFIGS[name]
@@ -361,43 +421,30 @@ def run_single(args):
     full = tuple(torch.broadcast_shapes(a_batch, b_batch))
     BN = math.prod(full)
     BA, BB = math.prod(a_batch), math.prod(b_batch)
-    a_idx = _batch_index(a_batch, full, dev)
-    b_idx = _batch_index(b_batch, full, dev)
-    A3 = a.reshape(BA, Mm, Kk)
-    B3 = b.reshape(BB, Kk, Nn)
     residual = _lib.OZ_RESIDUAL_COMPAT if s <= 4 else _lib.OZ_RESIDUAL_EXACT
-    alpha = oz.compute_split_bits(Kk, sd, oz.select_dot_accum_dtype(sd))
+    lib = _lib.load()
     gemm_events = []
+    # CUDA events for the GEMM launches of the timed steps, created up front
+    # (torch creates the underlying event at its first record)
+    ev_pool = []
+    for _ in range(args.steps + 4):
+        pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        for e in pair:
+            e.record(stream)
+        ev_pool.append(pair)
+    torch.cuda.synchronize()
 
     def step(record: bool):
-        """One ozaki_matmul, with the cross-GEMM timed by events."""
-        b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), Nn, Kk, s, alpha, sd, residual)
-        a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), Mm, Kk, s, alpha, sd, residual)
-        c = torch.empty((BN, Mm, Nn), dtype=dt, device=dev)
-        st = torch.cuda.current_stream()        # the capturing stream under --graph
+        """One public ozaki_matmul call; with ``record`` its cross-GEMM launch
+        is bracketed by a pair of CUDA events (oz_profile_next_gemm)."""
         if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-        _lib.check(_lib.load().oz_cross_gemm(
-            a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(), BN, Mm, Nn, Kk,
-            a_sl.shape[-1], s, _OZ_DTYPE[sd], _OZ_DTYPE[dt],
-            a_idx.data_ptr() if a_idx is not None else None,
-            b_idx.data_ptr() if b_idx is not None else None, BA, BB, c.data_ptr(), Nn, 0,
-            st.cuda_stream))
-        if record:
-            e1.record(st)
+            e0, e1 = ev_pool[len(gemm_events)]
+            lib.oz_profile_next_gemm(e0.cuda_event, e1.cuda_event)
             gemm_events.append((e0, e1))
-        return c
+        return oz.ozaki_matmul(a, b, num_splits=s, slice_dtype=sd)
 
     for _ in range(args.warmup):
         step(False)
-    # the timed step is the public call's work: check it once against the public call
-    c_api = oz.ozaki_matmul(a, b, num_splits=s, slice_dtype=sd)
-    c_step = step(False)
-    torch.cuda.synchronize()
-    assert torch.equal(c_api.reshape(c_step.shape), c_step)
-    del c_api
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -436,10 +483,17 @@ def run_single(args):
     value = flops / (ms * 1e-3) / 1e12
     pairs = s * s
     bf16_peak, hbm_peak, peak_src = peaks()
+    # the tensor peak of the slice dtype: B200's dense int8 rate is twice its
+    # bf16 rate, tf32 half; for int8 the rate cuBLAS reaches here is measured
+    # too and the larger of the two is the denominator
     tensor_peak = 2.0 * bf16_peak if sd == torch.int8 else (bf16_peak if sd != torch.float32
                                                             else bf16_peak / 2.0)
     peak_note = {torch.int8: "2x", torch.float16: "1x", torch.bfloat16: "1x",
                  torch.float32: "0.5x"}[sd]
+    int8_cublas = None
+    if sd == torch.int8 and not args.no_dgemm:
+        int8_cublas = int8_tensor_rate(dev)
+        tensor_peak = max(tensor_peak, int8_cublas)
     achieved = pairs * flops / (gemm_ms * 1e-3) / 1e12
 
     # accuracy against an fp64 matmul, and the native GEMM of the input dtype
@@ -491,6 +545,10 @@ def run_single(args):
                "d2h_bytes_per_step": c_pin.numel() * c_pin.element_size()}
 
     traffic = committed_traffic() if name == "C3" and s == 4 else None
+    clocks = clk.summary()
+    cpu_native = None
+    if not args.no_cpu_baseline:
+        cpu_native = cpu_native_matmul(a_h, b_h)
     line = {
         "metric": METRIC if name == "C3" else f"emulated TFLOPS (2MNK/t), {cfg['desc']}",
         "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps,
@@ -507,15 +565,28 @@ def run_single(args):
         "roofline": {"bound": "tensor", "kernel": f"cross_gemm_kernel<{SLICE_NAME[sd]}>",
                      "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
                      "frac": achieved / tensor_peak,
-                     "peak_source": f"{peak_note} {peak_src} dense bf16 ({bf16_peak} TF/s, "
-                                    "MEASURED_PEAKS.json); B200 dense int8 = 2x bf16, "
-                                    "tf32 = 0.5x",
+                     "peak_source": f"max of {peak_note} {peak_src} dense bf16 ({bf16_peak} TF/s, "
+                                    "MEASURED_PEAKS.json; B200 dense int8 = 2x bf16, "
+                                    "tf32 = 0.5x) and the int8 cuBLAS rate measured in this run",
+                     "frac_of_2x_bf16": (achieved / (2.0 * bf16_peak)
+                                         if sd == torch.int8 else None),
+                     "int8_cublas_tops": int8_cublas,
+                     "frac_of_int8_cublas": achieved / int8_cublas if int8_cublas else None,
                      "gemm_ms": gemm_ms,
+                     # the GEMM runs at the power cap: its time scaled to the
+                     # maximum SM clock by the median clock sampled meanwhile
+                     "gemm_ms_at_max_clock": (gemm_ms * clocks["sm_mhz"] / clocks["sm_max_mhz"]
+                                              if clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+                                              else None),
                      "traffic": traffic.get("cross_gemm_bytes_per_launch") if traffic else None},
         "rel_err_vs_fp64": rel_err,
         "native_gemm_tflops": native_tflops,
         "native_gemm": "cuBLAS DGEMM" if dt == torch.float64 else "cuBLAS SGEMM (no TF32)",
-        "clocks": clk.summary(),
+        "cpu_native_matmul": cpu_native,
+        "reference_triton_b200": ("unavailable: the reference has no setup.py or "
+                                  "pyproject.toml, so it cannot be installed for the GPU box, "
+                                  "and its sources are not copied into this repository"),
+        "clocks": clocks,
         "gpu_launches": launches,
         "e2e": e2e,
     }

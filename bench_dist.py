@@ -21,11 +21,11 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from . import dist as ozd
+from ozaki_triton_b200 import dist as ozd
 
 
 def main(args):
-    import bench  # the repository's bench.py (workload recipe, clocks, peaks)
+    import bench  # workload recipe, clock sampler, peaks
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))

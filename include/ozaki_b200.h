@@ -5,9 +5,14 @@
  * The library replaces the two device kernels of the reference
  * implementation WhFanatic/Ozaki_triton (ozaki_triton.py) and the wrappers
  * that launch them.  Every entry point takes plain device pointers, sizes,
- * strides and a CUDA stream; it never allocates, frees or synchronises, and
- * is re-entrant (no global state other than the last-error string, which is
- * thread-local, and the device-side timeout flag described below).
+ * strides and a CUDA stream.  No entry point allocates or frees device
+ * memory, and only oz_device_status synchronises (the stream it is given);
+ * the others only enqueue work on their stream.  State the library keeps:
+ * the last-error string (thread-local), the device-side timeout word of each
+ * kernel file (oz_device_status), a launch counter, and one static 32 MiB
+ * device array per GPU that only oz_split_noalloc uses.  Calls are
+ * re-entrant except that oz_split_noalloc calls overlapping on one GPU share
+ * that array.
  *
  * Status codes: 0 = OZ_OK; negative values are errors and oz_last_error()
  * returns a message for the calling thread.  Argument errors are reported
@@ -164,6 +169,38 @@ int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_sca
                   int64_t b_batches, void *c, int64_t ldc, uint32_t flags, void *stream);
 
 /*
+ * The whole product in one call.  Replaces ozaki_matmul
+ * (ozaki_triton.py:534-606) below its Python-level checks: B is split by
+ * columns (its transposed view, ozaki_triton.py:593) and A by rows into the
+ * workspace, then the fused cross-GEMM writes C in the input dtype
+ * (ozaki_triton.py:575, 606).  alpha comes from oz_compute_split_bits(k).
+ *
+ *   a : element (b, i, kk) at a + b*a_sb + i*a_sm + kk*a_sk (element strides),
+ *       a_batches matrices (m, k); b : element (b, kk, j) at
+ *       b + b*b_sb + kk*b_sk + j*b_sn, b_batches matrices (k, n).  Any strides.
+ *   batch, a_index, b_index : output batches and the operand members each uses
+ *       (NULL = identity), as in oz_cross_gemm: torch.matmul broadcasting
+ *       without copies of the operands.
+ *   c : (batch, m, n) of in_dtype, row pitch ldc.
+ *   workspace : oz_matmul_workspace_bytes() bytes of device memory, 256-byte
+ *       aligned (slices, scales and the column-transpose scratch).
+ * Small operand pairs (A and B together at most 4 Mi elements, k * 8 bytes
+ * at most 48 KB) are split in a single launch, so the call is two kernels;
+ * larger ones take the streaming split kernels (three or more).  Results are
+ * bit-identical either way.
+ */
+int64_t oz_matmul_workspace_bytes(int in_dtype, int64_t a_batches, int64_t b_batches, int64_t m,
+                                  int64_t n, int64_t k, int64_t a_sm, int64_t a_sk, int64_t b_sk,
+                                  int64_t b_sn, int32_t num_splits, int slice_dtype);
+
+int oz_matmul(const void *a, const void *b, int in_dtype, int64_t batch, int64_t a_batches,
+              int64_t b_batches, const int32_t *a_index, const int32_t *b_index, int64_t m,
+              int64_t n, int64_t k, int64_t a_sb, int64_t a_sm, int64_t a_sk, int64_t b_sb,
+              int64_t b_sk, int64_t b_sn, int32_t num_splits, int slice_dtype, int residual_mode,
+              void *c, int64_t ldc, uint32_t flags, void *workspace, int64_t workspace_bytes,
+              void *stream);
+
+/*
  * oz_cross_gemm with B's slices stored in column blocks (no counterpart in the
  * reference, which has no multi-GPU path; this is the layout an all-gather or
  * a blockwise broadcast of B's slices produces without a re-layout copy).
@@ -212,6 +249,15 @@ int oz_copy_async(void *dst, const void *src, int64_t bytes, void *stream);
  * OZ_ERR_TIMEOUT, writes the recorded code (0 = none) to *code, and clears it.
  */
 int oz_device_status(void *stream, int32_t *code);
+
+/*
+ * Kernel timing from the caller's side (no counterpart in the reference):
+ * the next cross-GEMM launch made by this thread (through oz_cross_gemm,
+ * oz_cross_gemm_blocked or oz_matmul) records begin_event just before it and
+ * end_event just after it, on the launch's stream; then the pair is
+ * forgotten.  Either may be NULL.  The events are the caller's cudaEvent_t.
+ */
+int oz_profile_next_gemm(void *begin_event, void *end_event);
 
 /* Kernels the library has launched in this process, a running total (no
  * counterpart in the reference; lets a caller count the device work of a

@@ -41,12 +41,18 @@ SIGNATURES = {
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_cross_gemm_blocked": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int,
                                      _int, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _u32, _vp]),
+    "oz_matmul_workspace_bytes": (_i64, [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                         _i64, _i32, _int]),
+    "oz_matmul": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64,
+                         _i64, _i64, _i64, _i64, _i64, _i32, _int, _int, _vp, _i64, _u32, _vp,
+                         _i64, _vp]),
     "oz_ipc_export": (_int, [_vp, _vp, ctypes.POINTER(_i64)]),
     "oz_ipc_import": (_int, [_vp, _i64, ctypes.POINTER(_vp)]),
     "oz_ipc_close": (_int, [_vp, _i64]),
     "oz_copy_async": (_int, [_vp, _vp, _i64, _vp]),
     "oz_device_status": (_int, [_vp, ctypes.POINTER(_i32)]),
     "oz_launch_count": (_i64, []),
+    "oz_profile_next_gemm": (_int, [_vp, _vp]),
     "oz_wait_selftest": (_int, [_i64, _vp]),
     "oz_last_error": (ctypes.c_char_p, []),
     "oz_version": (ctypes.c_char_p, []),

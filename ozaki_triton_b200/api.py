@@ -233,6 +233,25 @@ def cross_gemm(A_slices: torch.Tensor, B_slices: torch.Tensor, A_scales: torch.T
     return C
 
 
+def broadcast_batch(a: Tuple[int, ...], b: Tuple[int, ...]) -> Tuple[int, ...]:
+    """torch.broadcast_shapes of two batch shapes (ozaki_triton.py:518), as plain
+    tuple arithmetic: the torch call costs about 0.1 ms of host time, more
+    than a whole small product on the GPU.  Raises RuntimeError like torch."""
+    n = max(len(a), len(b))
+    pa = (1,) * (n - len(a)) + tuple(a)
+    pb = (1,) * (n - len(b)) + tuple(b)
+    out = []
+    for x, y in zip(pa, pb):
+        if x == y or y == 1:
+            out.append(x)
+        elif x == 1:
+            out.append(y)
+        else:
+            raise RuntimeError(f"Shape mismatch: objects cannot be broadcast to a single shape. "
+                               f"Mismatch is between {tuple(a)} and {tuple(b)}.")
+    return tuple(out)
+
+
 def _batch_index(own: Tuple[int, ...], full: Tuple[int, ...], device) -> Optional[torch.Tensor]:
     """Member of an operand with batch shape ``own`` used by each batch of ``full``."""
     if tuple(own) == tuple(full):
@@ -267,7 +286,7 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     input_dtype = A.dtype
     dot_accum_dtype = select_dot_accum_dtype(slice_dtype)
     a_batch, b_batch = tuple(A.shape[:-2]), tuple(B.shape[:-2])
-    batch_shape = tuple(torch.broadcast_shapes(a_batch, b_batch))
+    batch_shape = broadcast_batch(a_batch, b_batch)
     BN = math.prod(batch_shape)
     out_shape = (*batch_shape, M, N)
     if BN == 0:
@@ -283,27 +302,27 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     if M == 0 or N == 0:
         return torch.empty(out_shape, dtype=input_dtype, device=A.device)
     mode = _residual_mode(residual, num_splits, input_dtype)
-    # split each distinct batch member once (no broadcast copies)
+    # each distinct batch member is split once (no broadcast copies); one
+    # library call splits B by columns and A by rows into the workspace and
+    # runs the fused cross-GEMM
     A3 = A.reshape(math.prod(a_batch), M, K)
     B3 = B.reshape(math.prod(b_batch), K, N)
-    # B is split by columns: lines = N (stride 1 when B is row-major), k stride = N
-    b_sl, b_sc = _split_lines(B3, B3.stride(2), B3.stride(1), N, K, num_splits, alpha,
-                              slice_dtype, mode)
-    a_sl, a_sc = _split_lines(A3, A3.stride(1), A3.stride(2), M, K, num_splits, alpha,
-                              slice_dtype, mode)
     a_idx = _batch_index(a_batch, batch_shape, A.device)
     b_idx = _batch_index(b_batch, batch_shape, A.device)
-
-    C = torch.empty((BN, M, N), dtype=input_dtype, device=A.device)
     lib = _lib.load()
-    ld = a_sl.shape[-1]
-    _lib.check(lib.oz_cross_gemm(
-        a_sl.data_ptr(), b_sl.data_ptr(), a_sc.data_ptr(), b_sc.data_ptr(),
-        BN, M, N, K, ld, num_splits, _OZ_DTYPE[slice_dtype], _OZ_DTYPE[input_dtype],
+    code, scode = _OZ_DTYPE[input_dtype], _OZ_DTYPE[slice_dtype]
+    ws_bytes = lib.oz_matmul_workspace_bytes(code, A3.shape[0], B3.shape[0], M, N, K,
+                                             A3.stride(1), A3.stride(2), B3.stride(1),
+                                             B3.stride(2), num_splits, scode)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
+    C = torch.empty((BN, M, N), dtype=input_dtype, device=A.device)
+    _lib.check(lib.oz_matmul(
+        A3.data_ptr(), B3.data_ptr(), code, BN, A3.shape[0], B3.shape[0],
         a_idx.data_ptr() if a_idx is not None else None,
-        b_idx.data_ptr() if b_idx is not None else None,
-        A3.shape[0], B3.shape[0], C.data_ptr(), N,
-        _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0, _stream_ptr(A.device)))
+        b_idx.data_ptr() if b_idx is not None else None, M, N, K,
+        A3.stride(0), A3.stride(1), A3.stride(2), B3.stride(0), B3.stride(1), B3.stride(2),
+        num_splits, scode, mode, C.data_ptr(), N, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
+        ws.data_ptr(), ws_bytes, _stream_ptr(A.device)))
     return C.view(out_shape)
 
 

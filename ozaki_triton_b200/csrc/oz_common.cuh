@@ -31,6 +31,17 @@ static __device__ int g_device_status = 0;
 int status_split(int *value, bool clear);
 int status_gemm(int *value, bool clear);
 
+// Split of both operands of a product in one launch (oz_split.cu): A's rows
+// (a_sm, a_sk: line and k strides) and B's columns (b_sn, b_sk), each into
+// its own slices (batch, s, lines, ld) and scales.  Sets *done only when the
+// operands are small enough for it; otherwise nothing is launched.
+int split_two_small_impl(int in_dtype, const void *a, int64_t a_batches, int64_t m, int64_t a_sb,
+                         int64_t a_sm, int64_t a_sk, const void *b, int64_t b_batches, int64_t n,
+                         int64_t b_sb, int64_t b_sn, int64_t b_sk, int64_t k, int32_t s,
+                         int32_t alpha, int slice_dtype, int residual_mode, void *a_slices,
+                         float *a_scales, void *b_slices, float *b_scales, int64_t ld,
+                         void *stream, bool *done);
+
 // Read (and optionally clear) this translation unit's status word.
 static inline int read_status_word(int *value, bool clear) {
   int v = 0;

@@ -549,6 +549,10 @@ TileChoice choose_tile(int64_t m, int s) {
   return t;
 }
 
+// Events recorded around the next cross-GEMM launch of this thread
+// (oz_profile_next_gemm), then forgotten.
+thread_local cudaEvent_t g_prof_begin = nullptr, g_prof_end = nullptr;
+
 }  // namespace
 int status_gemm(int *value, bool clear) { return read_status_word(value, clear); }
 
@@ -651,12 +655,19 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
                                  stage_bytes(num_splits, nt, pair));
 
   const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
-  if (pair == 2) {
-    if (nt == 128) return launch_kind<128, 2>(kind, out_dtype, ta, tb, p, st);
-    return launch_kind<64, 2>(kind, out_dtype, ta, tb, p, st);
-  }
-  if (nt == 128) return launch_kind<128, 1>(kind, out_dtype, ta, tb, p, st);
-  return launch_kind<64, 1>(kind, out_dtype, ta, tb, p, st);
+  cudaEvent_t ev0 = g_prof_begin, ev1 = g_prof_end;
+  g_prof_begin = g_prof_end = nullptr;
+  if (ev0)
+    if (int rc = check_cuda(cudaEventRecord(ev0, st), "cudaEventRecord(profile begin)")) return rc;
+  int rc;
+  if (pair == 2)
+    rc = nt == 128 ? launch_kind<128, 2>(kind, out_dtype, ta, tb, p, st)
+                   : launch_kind<64, 2>(kind, out_dtype, ta, tb, p, st);
+  else
+    rc = nt == 128 ? launch_kind<128, 1>(kind, out_dtype, ta, tb, p, st)
+                   : launch_kind<64, 1>(kind, out_dtype, ta, tb, p, st);
+  if (rc == OZ_OK && ev1) rc = check_cuda(cudaEventRecord(ev1, st), "cudaEventRecord(profile end)");
+  return rc;
 }
 
 }  // namespace
@@ -687,6 +698,12 @@ extern "C" int oz_wait_selftest(int64_t bound_cycles, void *stream) {
   wait_selftest_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       (long long)bound_cycles);
   return check_cuda(cudaGetLastError(), "wait_selftest_kernel launch");
+}
+
+extern "C" int oz_profile_next_gemm(void *begin_event, void *end_event) {
+  oz::g_prof_begin = reinterpret_cast<cudaEvent_t>(begin_event);
+  oz::g_prof_end = reinterpret_cast<cudaEvent_t>(end_event);
+  return OZ_OK;
 }
 
 extern "C" int oz_cross_gemm(const void *a_slices, const void *b_slices, const float *a_scales,

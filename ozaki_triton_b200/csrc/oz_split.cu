@@ -963,6 +963,69 @@ __global__ void __launch_bounds__(kAnyThreads)
 }
 
 // ---------------------------------------------------------------------------
+// both operands of a small product in one launch
+// ---------------------------------------------------------------------------
+// One CTA per line of A (rows) or of B (columns), in one grid: blocks
+// [0, a.batch * a.lines) take A's lines, the rest B's.  The line is read once
+// into shared memory in the residual precision and every level works there
+// with the generic kernel's per-element arithmetic (quant_step), so the
+// slices are the same bits as every other split kernel's.  Used for products
+// whose operands are small (launch latency, not bandwidth, is their cost).
+struct LineSet {
+  const void *in;
+  int64_t stride_b, stride_line, stride_k;
+  int64_t batch, lines;
+  void *slices;
+  float *scales;
+};
+constexpr int kPairSmallThreads = 256;
+
+template <typename TIn, int SK, bool EXACT>
+__global__ void __launch_bounds__(kPairSmallThreads)
+    split_two_small(const LineSet a, const LineSet b, int K, int ld, int s, int alpha) {
+  using RD = typename RdOf<TIn>::type;
+  using ST = typename SliceT<SK>::type;
+  extern __shared__ __align__(16) unsigned char smem_small[];
+  RD *res = reinterpret_cast<RD *>(smem_small);
+  __shared__ float red[kPairSmallThreads / 32];
+  const int64_t na = a.batch * a.lines;
+  const bool is_a = (int64_t)blockIdx.x < na;
+  const LineSet &op = is_a ? a : b;
+  const int64_t flat = is_a ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - na;
+  const int64_t bb = flat / op.lines, line = flat - bb * op.lines;
+  const TIn *src = reinterpret_cast<const TIn *>(op.in) + bb * op.stride_b + line * op.stride_line;
+  for (int k = threadIdx.x; k < K; k += kPairSmallThreads)
+    res[k] = in_to_rd<TIn, RD>(src[(int64_t)k * op.stride_k]);
+  __syncthreads();
+  ST *dst = reinterpret_cast<ST *>(op.slices) + (bb * s * op.lines + line) * (int64_t)ld;
+  for (int l = 0; l < s; ++l) {
+    float m = 0.f;
+    for (int k = threadIdx.x; k < K; k += kPairSmallThreads) m = fmaxf(m, abs_to_f32<RD>(res[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int i = 1; i < kPairSmallThreads / 32; ++i) m = fmaxf(m, red[i]);
+    Level<RD> lv;
+    lv.init(m, alpha);
+    if (threadIdx.x == 0) op.scales[(bb * s + l) * op.lines + line] = lv.scale;
+    ST *dl = dst + (int64_t)l * op.lines * ld;
+    for (int k = threadIdx.x; k < ld; k += kPairSmallThreads) {
+      if (k < K) {
+        RD r = res[k];
+        dl[k] = quant_step<SK, RD, EXACT>(r, lv, l < s - 1);
+        res[k] = r;
+      } else {
+        dl[k] = ST(0.0f);
+      }
+    }
+    __syncthreads();   // red[] and res[] reused by the next level
+  }
+}
+
+// ---------------------------------------------------------------------------
 // transpose of contiguous lines into a K-contiguous workspace
 // ---------------------------------------------------------------------------
 // ws[(b * lines + n) * kp + k] = in[b * stride_b + k * stride_k + n] for k < K,
@@ -1026,6 +1089,27 @@ int launch_rows_nc(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lin
   return check_cuda(cudaGetLastError(), "split_rows_tma launch");
 }
 
+// Whether two CTAs of the 256-thread fp64 row kernel are resident on one SM
+// with the largest dynamic shared memory that path requests (then any
+// smaller request fits too).  Asked once per kernel instance: every GPU this
+// library runs on is a B200.
+template <typename TIn, int SK, bool EXACT>
+bool rows_two_ctas_resident() {
+  static const bool ok = [] {
+    auto kern = split_rows_tma<TIn, SK, 256, 8, EXACT, 256>;
+    const int smem = kRowSmem / 2 + kRowMaxStages * 8 + 2 * 16 * 4;
+    int blocks = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, 256, smem) != cudaSuccess) {
+      (void)cudaGetLastError();   // the failed query's error, not a kernel's
+      return false;
+    }
+    return blocks >= 2;
+  }();
+  return ok;
+}
+
 template <typename TIn, int SK, bool EXACT>
 int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K, int ld,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
@@ -1062,15 +1146,16 @@ int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines,
   if constexpr (sizeof(TIn) == 8) {
     // fp64 rows of up to 8192 elements: two 256-thread CTAs per SM, one row
     // each -- two independent barrier domains per SM instead of one (0.228
-    // vs 0.264 ms for 8192^2 with 4 int8 slices).  OZ_SPLIT_ROWS_CTA=512
-    // selects the single 512-thread CTA (benchmarking only).
-    static const bool two = [] {
-      const char *e = getenv("OZ_SPLIT_ROWS_CTA");
-      return !(e && atoi(e) == 512);
-    }();
+    // vs 0.264 ms for 8192^2 with 4 int8 slices).  The kernel needs 128
+    // registers per thread (ptxas, 20 bytes of spill), so two CTAs fill the
+    // register file exactly; if fewer than two are resident, or
+    // OZ_SPLIT_ROWS_CTA=512 is set (read on every call), the single
+    // 512-thread CTA per SM runs instead.
+    const char *env = getenv("OZ_SPLIT_ROWS_CTA");
+    const bool two = !(env && atoi(env) == 512);
     if (two && c512 <= 4) {
       const int NS = std::min(kRowMaxStages, (kRowSmem / 2) / rowp);
-      if (NS >= 1) {
+      if (NS >= 1 && rows_two_ctas_resident<TIn, SK, EXACT>()) {
         *done = true;
         return launch_rows_nc<TIn, SK, EXACT, 256, 8, 256>(in, sb, sl, batch, lines, K, ld, s,
                                                           alpha, slices, scales, st, NS, rowp);
@@ -1467,7 +1552,70 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
   }
 }
 
+template <typename TIn, int SK, bool EXACT>
+int launch_two_small(const LineSet &a, const LineSet &b, int K, int ld, int s, int alpha,
+                     cudaStream_t st) {
+  using RD = typename RdOf<TIn>::type;
+  const int64_t blocks = a.batch * a.lines + b.batch * b.lines;
+  const int smem = K * (int)sizeof(RD);
+  count_launch();
+  split_two_small<TIn, SK, EXACT><<<(unsigned)blocks, kPairSmallThreads, smem, st>>>(
+      a, b, K, ld, s, alpha);
+  return check_cuda(cudaGetLastError(), "split_two_small launch");
+}
+
+template <typename TIn>
+int two_small_slice(int slice_dtype, bool exact, const LineSet &a, const LineSet &b, int K, int ld,
+                    int s, int alpha, cudaStream_t st) {
+#define OZ_T(SK)                                                                              \
+  return exact ? launch_two_small<TIn, SK, true>(a, b, K, ld, s, alpha, st)                    \
+               : launch_two_small<TIn, SK, false>(a, b, K, ld, s, alpha, st);
+  switch (slice_dtype) {
+    case OZ_I8: OZ_T(OZ_I8)
+    case OZ_F16: OZ_T(OZ_F16)
+    case OZ_BF16: OZ_T(OZ_BF16)
+    case OZ_F32: OZ_T(OZ_F32)
+  }
+#undef OZ_T
+  return set_error(OZ_ERR_UNSUPPORTED, "unsupported slice dtype %d", slice_dtype);
+}
+
 }  // namespace
+
+// Largest operand pair (elements of A and B together) and line length the
+// one-launch split takes: below this the split is launch-bound, and a line
+// of the residual fits the default 48 KB of shared memory.
+constexpr int64_t kTwoSmallMaxElems = 1ll << 22;
+constexpr int64_t kTwoSmallMaxLineBytes = 48 * 1024;
+
+int split_two_small_impl(int in_dtype, const void *a, int64_t a_batches, int64_t m, int64_t a_sb,
+                         int64_t a_sm, int64_t a_sk, const void *b, int64_t b_batches, int64_t n,
+                         int64_t b_sb, int64_t b_sn, int64_t b_sk, int64_t k, int32_t s,
+                         int32_t alpha, int slice_dtype, int residual_mode, void *a_slices,
+                         float *a_scales, void *b_slices, float *b_scales, int64_t ld,
+                         void *stream, bool *done) {
+  *done = false;
+  const int rd_bytes = in_dtype == OZ_F64 ? 8 : 4;
+  const int64_t lines = a_batches * m + b_batches * n;
+  if (k < 1 || k * rd_bytes > kTwoSmallMaxLineBytes || lines * k > kTwoSmallMaxElems ||
+      lines > INT32_MAX || ld > INT32_MAX || s < 1 || s > kMaxSplits)
+    return OZ_OK;
+  LineSet la{a, a_sb, a_sm, a_sk, a_batches, m, a_slices, a_scales};
+  LineSet lb{b, b_sb, b_sn, b_sk, b_batches, n, b_slices, b_scales};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool exact = residual_mode == OZ_RESIDUAL_EXACT && in_dtype == OZ_F64;
+  *done = true;
+  switch (in_dtype) {
+    case OZ_F64: return two_small_slice<double>(slice_dtype, exact, la, lb, (int)k, (int)ld, s, alpha, st);
+    case OZ_F32: return two_small_slice<float>(slice_dtype, exact, la, lb, (int)k, (int)ld, s, alpha, st);
+    case OZ_F16: return two_small_slice<__half>(slice_dtype, exact, la, lb, (int)k, (int)ld, s, alpha, st);
+    case OZ_BF16: return two_small_slice<__nv_bfloat16>(slice_dtype, exact, la, lb, (int)k, (int)ld, s, alpha, st);
+    case OZ_I8: return two_small_slice<int8_t>(slice_dtype, exact, la, lb, (int)k, (int)ld, s, alpha, st);
+  }
+  *done = false;
+  return set_error(OZ_ERR_UNSUPPORTED, "unsupported input dtype %d", in_dtype);
+}
+
 }  // namespace oz
 
 extern "C" int oz_split(const void *in, int in_dtype, int64_t batch, int64_t lines, int64_t k,

@@ -40,6 +40,7 @@ from .api import (
     _batch_index,
     _residual_mode,
     _split_lines,
+    broadcast_batch,
     compute_split_bits,
     select_dot_accum_dtype,
 )
@@ -525,7 +526,7 @@ def ozaki_matmul_batches(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     K2, N = B.shape[-2:]
     assert K == K2
     a_batch, b_batch = tuple(A.shape[:-2]), tuple(B.shape[:-2])
-    full = tuple(torch.broadcast_shapes(a_batch, b_batch))
+    full = broadcast_batch(a_batch, b_batch)
     bn = math.prod(full)
     start, stop = block_range(bn, world, rank)
     alpha = compute_split_bits(K, slice_dtype=slice_dtype,

@@ -57,6 +57,27 @@ def test_split_matches_reference_golden(case):
                      want if sk == "int8" else want.astype(np.float64))
 
 
+@pytest.mark.parametrize("cta", ["256", "512"])
+@pytest.mark.parametrize("name", ["rows_f64_i8_s4_k8192", "cols_f64_i8_s2_k4100"])
+def test_split_fp64_row_kernel_both_cta_shapes(name, cta, monkeypatch):
+    """fp64 rows of up to 8192 elements run on two 256-thread CTAs per SM by
+    default, or on one 512-thread CTA (OZ_SPLIT_ROWS_CTA=512, read on every
+    call; the same kernel is the fallback when two CTAs are not resident).
+    Both are bit-exact on the K = 8192 and K = 4100 goldens, presented as
+    contiguous rows."""
+    monkeypatch.setenv("OZ_SPLIT_ROWS_CTA", cta)
+    case = next(c for c in SPLITS if c["name"] == name)
+    x = case["x"] if case["layout"] == "rows" else np.swapaxes(case["x"], -1, -2)
+    xd = to_dev(np.ascontiguousarray(x), "fp64")
+    from ozaki_triton_b200 import _lib
+    n0 = _lib.load().oz_launch_count()
+    sl, sc = oz.split_matrix(xd, case["s"], case["alpha"], torch.int8)
+    torch.cuda.synchronize()
+    assert _lib.load().oz_launch_count() - n0 == 1      # the row kernel, no generic fallback
+    assert same_bits(host(sc), case["scales"])
+    assert same_bits(host(sl), case["slices"])
+
+
 MATMULS = matmul_cases()
 
 
@@ -340,16 +361,44 @@ def test_bounded_wait_times_out_and_the_context_stays_usable():
 
 
 def test_launch_count_of_a_matmul():
-    """oz_launch_count: an fp64 matmul is three library kernels (split of A's
-    rows, column-pair split of B, cross-GEMM) -- the count bench.py reports."""
+    """oz_launch_count: a small fp64 matmul is two library kernels (both
+    operands split in one launch, then the cross-GEMM); one with long rows
+    (K = 8192: 64 KB fp64 lines) is three (split of A's rows, column-pair
+    split of B, cross-GEMM) -- the count bench.py reports."""
     from ozaki_triton_b200 import _lib
     rng = np.random.default_rng(3)
-    a = to_dev(rng.standard_normal((512, 512)), "fp64")
-    b = to_dev(rng.standard_normal((512, 256)), "fp64")
     lib = _lib.load()
-    n0 = lib.oz_launch_count()
-    oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.int8)
-    assert lib.oz_launch_count() - n0 == 3
+    for (m, k, n), want in [((512, 512, 256), 2), ((256, 8192, 256), 3)]:
+        a = to_dev(rng.standard_normal((m, k)), "fp64")
+        b = to_dev(rng.standard_normal((k, n)), "fp64")
+        n0 = lib.oz_launch_count()
+        oz.ozaki_matmul(a, b, num_splits=2, slice_dtype=torch.int8)
+        assert lib.oz_launch_count() - n0 == want, (m, k, n)
+
+
+@pytest.mark.parametrize("ik,sk,s", [("fp64", "int8", 4), ("fp64", "fp16", 3), ("fp32", "fp16", 2),
+                                     ("fp32", "int8", 3), ("bf16", "fp32", 2), ("fp16", "bf16", 2),
+                                     ("int8", "int8", 2), ("fp64", "int8", 8)])
+@pytest.mark.parametrize("shape", [(3, 100, 70, 300), (1, 1024, 768, 1024), (2, 33, 40, 5000)])
+def test_one_launch_split_matches_streaming_kernels(ik, sk, s, shape):
+    """ozaki_matmul splits small operand pairs in one launch (one CTA per
+    line, the line held in shared memory).  Its C is the same bits as the
+    product of the separately launched streaming split kernels (split_matrix
+    of A's rows and of B's transposed view, then cross_gemm)."""
+    bn, m, n, k = shape
+    rng = np.random.default_rng(m + n + k)
+    a = to_dev(rand_lines(rng, (bn, m, k), ik), ik)
+    b = to_dev(rand_lines(rng, (bn, k, n), ik), ik)
+    got = oz.ozaki_matmul(a, b, num_splits=s, slice_dtype=TDT[sk])
+    alpha = oz.compute_split_bits(k, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    mode = "compat" if s <= 4 else "exact"
+    a_sl, a_sc = oz.split_matrix(a, s, alpha, TDT[sk], residual=mode)
+    b_sl, b_sc = oz.split_matrix(b.transpose(-1, -2), s, alpha, TDT[sk], residual=mode)
+    want = oz.cross_gemm(a_sl, b_sl.transpose(-1, -2), a_sc, b_sc, s, a.dtype)
+    torch.cuda.synchronize()
+    assert oz.device_status() == 0
+    assert torch.equal(got.view(torch.uint8) if got.dtype != torch.int8 else got,
+                       want.view(torch.uint8) if want.dtype != torch.int8 else want)
 
 
 def test_int8_inputs_saturate_out_of_range():

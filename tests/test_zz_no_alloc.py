@@ -54,6 +54,45 @@ def test_noalloc_split_matches_workspace_split_twice():
         assert torch.equal(got_sc, want_sc)
 
 
+@pytest.mark.parametrize("K,N,batch", [(9000, 300, 1), (1000, 301, 2)])
+def test_noalloc_transposes_into_the_fixed_array(K, N, batch):
+    """Inputs that no column kernel takes go through the fixed array: fp64
+    columns with K > 8192 (beyond the column-pair kernel's four 2048-row
+    chunks), or an odd column count (a row pitch that is not a multiple of 16
+    bytes, which TMA cannot address).  They are transposed into the array and
+    split as rows: two launches.  Two calls in a row with different data (the
+    second finds the first call's values in the array) give the same bits as
+    oz_split_ex with a caller workspace, and as the CPU oracle."""
+    import oracle
+    from ozaki_triton_b200 import _lib
+    lib = _lib.load()
+    s = 4
+    alpha = int(oracle.compute_split_bits(K, "int8", "int32"))
+    need = lib.oz_split_workspace_bytes(_lib.OZ_F64, batch, N, K, 1, N)
+    assert 0 < need <= lib.oz_split_noalloc_max_bytes()
+    g = torch.Generator().manual_seed(K + N)
+    for call, scale in enumerate((1e-3, 1e4)):
+        x_h = (torch.rand(batch, K, N, generator=g, dtype=torch.float64) - 0.5) * torch.exp(
+            2.0 * torch.randn(batch, K, N, generator=g, dtype=torch.float64)) * scale
+        x = x_h.to(DEV)
+        # the workspace starts as a sentinel: oz_split_ex must overwrite it
+        # (the transpose ran), like oz_split_noalloc overwrites the array
+        ws = torch.full((need,), 0xFF, dtype=torch.uint8, device=DEV)
+        want_sl, want_sc = _run(lib, lib.oz_split_ex, x, K, N, s, alpha, ws)
+        assert not bool((ws == 0xFF).all())
+        n0 = lib.oz_launch_count()
+        got_sl, got_sc = _run(lib, lib.oz_split_noalloc, x, K, N, s, alpha)
+        assert lib.oz_launch_count() - n0 == 2, "transpose + row split expected"
+        assert torch.equal(got_sl, want_sl), f"call {call}: slices differ"
+        assert torch.equal(got_sc, want_sc), f"call {call}: scales differ"
+        lines = np.swapaxes(x_h.numpy(), -1, -2)
+        rsl, rsc = oracle.split_lines(lines, s, alpha, "int8", "fp64")
+        got = got_sl.cpu().numpy()
+        assert np.array_equal(got[..., :K], rsl), f"call {call}: slices differ from the oracle"
+        assert not got[..., K:].any(), "slice row padding must be zero"
+        assert np.array_equal(got_sc.cpu().numpy().view(np.uint32), rsc.view(np.uint32))
+
+
 def test_noalloc_rejects_inputs_beyond_the_scratch():
     from ozaki_triton_b200 import _lib
     lib = _lib.load()
