@@ -283,6 +283,9 @@ def main():
     ap.add_argument("--dist", default="sharded", choices=["sharded", "root"],
                     help="multi-GPU data layout: A rows x B column panels with an all-gather "
                          "of B's slices (sharded), or B on rank 0 broadcast (root)")
+    ap.add_argument("--alt-steps", type=int, default=5,
+                    help="multi-GPU: timed steps of the other layout and of the gather of C "
+                         "to rank 0 (0 = skip)")
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS),
                     help="benchmark configuration (C3 = the headline)")
     ap.add_argument("--num-splits", type=int, default=0, help="override the config's s")

@@ -19,7 +19,7 @@ PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "liboz_b200.so")
 UNITS = ["oz_api.cu", "oz_split.cu", "oz_gemm.cu", "oz_peer.cu"]
-SOURCES = UNITS + ["oz_common.cuh", "oz_log2_table.h"]
+SOURCES = UNITS + ["oz_common.cuh", "oz_log2_table.h", "oz_tile_table.h"]
 BUILD_DIR = os.path.join(PKG, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -32,6 +32,7 @@
 #include <cudaTypedefs.h>
 
 #include "oz_common.cuh"
+#include "oz_tile_table.h"
 
 namespace oz {
 
@@ -529,15 +530,34 @@ int launch_kind(int kind, int out_dtype, const CUtensorMap &ta, const CUtensorMa
   return launch_out<2, NT, PAIR>(out_dtype, ta, tb, p, st);
 }
 
-// The tile table (it replaces the reference's Optuna autotuner): NT columns
-// per tile so that the s accumulators of one pass fit the 512 TMEM columns,
-// and CTA pairs (256-row tiles, half the B traffic per CTA) unless M fits one
-// 128-row tile.  OZ_GEMM_TILE="pair,nt" overrides it (benchmarking only).
-struct TileChoice { int pair, nt; };
-TileChoice choose_tile(int64_t m, int s) {
-  TileChoice t;
-  t.nt = s <= 4 ? 128 : 64;
-  t.pair = m > kBM ? 2 : 1;
+// Tile shape, raster group and pipeline depth of one launch: the committed
+// table (oz_tile_table.h) for the shapes it lists; otherwise NT columns so
+// that the s accumulators of one pass fit the 512 TMEM columns, CTA pairs
+// (256-row tiles, half the B traffic per CTA) unless M fits one 128-row tile,
+// and single-CTA 64-column tiles when a pair grid would leave more than half
+// of the SMs idle (they spread a small product over the whole GPU: 0.15 vs
+// 0.24 ms for 1024 x 1024 x 8192, s = 4).  OZ_GEMM_TILE="pair,nt" and
+// OZ_GEMM_GM override the choice (benchmarking only).
+struct TileChoice { int pair, nt, gm, stages; };
+TileChoice choose_tile(int kind, int s, int64_t batch, int64_t m, int64_t n, int64_t k) {
+  TileChoice t{0, 0, 16, 0};
+  bool listed = false;
+  for (const TileEntry &e : kTileTable)
+    if (e.kind == kind && e.s == s && e.batch == batch && e.m == m && e.n == n && e.k == k &&
+        s * e.nt <= 512) {
+      t = TileChoice{e.pair, e.nt, e.gm, e.stages};
+      listed = true;
+      break;
+    }
+  if (!listed) {
+    t.nt = s <= 4 ? 128 : 64;
+    t.pair = m > kBM ? 2 : 1;
+    const int64_t pair_tiles = batch * ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + t.nt - 1) / t.nt);
+    if (t.pair == 2 && pair_tiles * 2 * 2 <= sm_count()) {
+      t.pair = 1;
+      t.nt = 64;
+    }
+  }
   if (const char *env = getenv("OZ_GEMM_TILE")) {
     int pr = 0, nt = 0;
     if (sscanf(env, "%d,%d", &pr, &nt) == 2 && (pr == 1 || pr == 2) && (nt == 64 || nt == 128) &&
@@ -545,6 +565,10 @@ TileChoice choose_tile(int64_t m, int s) {
       t.pair = pr;
       t.nt = nt;
     }
+  }
+  if (const char *env = getenv("OZ_GEMM_GM")) {
+    const int g = atoi(env);
+    if (g >= 1 && g <= 64) t.gm = g;
   }
   return t;
 }
@@ -612,7 +636,8 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
       b_batches * bblocks * num_splits > INT32_MAX)
     return set_error(OZ_ERR_INVALID, "size out of range");
 
-  const TileChoice tc = choose_tile(m, num_splits);
+  const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
+  const TileChoice tc = choose_tile(kind, num_splits, batch, m, n, k);
   const int nt = tc.nt, pair = tc.pair;
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, a_slices, (uint64_t)ld_bytes, (uint64_t)m,
@@ -642,19 +667,15 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   p.tiles_n = (int)((n + nt - 1) / nt);
   p.bw = (int)bw;
   p.bblocks = (int)bblocks;
-  p.gm = 16;
-  if (const char *env = getenv("OZ_GEMM_GM")) {
-    const int g = atoi(env);
-    if (g >= 1 && g <= 64) p.gm = g;
-  }
+  p.gm = tc.gm;
   int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
   p.idesc = make_idesc(slice_dtype, kBM * pair);
   p.stages = min(kMaxStages, (kSmemBudget - scale_stage_bytes(num_splits, nt)) /
                                  stage_bytes(num_splits, nt, pair));
+  if (tc.stages > 0 && tc.stages < p.stages) p.stages = tc.stages;
 
-  const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
   cudaEvent_t ev0 = g_prof_begin, ev1 = g_prof_end;
   g_prof_begin = g_prof_end = nullptr;
   if (ev0)

@@ -160,10 +160,52 @@ def _split_block(backend, Bc: torch.Tensor, k: int, num_splits: int, alpha: int,
         sc_block[:, :nc].copy_(t_sc[0])
 
 
+def gather_rows(c_local: torch.Tensor, root: int = 0, group=None,
+                rows: Optional[list] = None) -> Optional[torch.Tensor]:
+    """Row blocks of C from every rank to ``root``, in rank order.
+
+    ``c_local`` is this rank's (M_r, N) block (M_r may differ per rank,
+    including 0).  Returns the whole (sum M_r, N) matrix on ``root`` and None
+    elsewhere.  ``rows`` (every rank's M_r) saves one small all-gather when
+    the caller knows it.  Point-to-point sends of contiguous row blocks (NCCL
+    on GPUs, gloo on CPU), one per rank, all posted at once.  The reference
+    returns the whole C on the caller's device (ozaki_triton.py:604-606);
+    this is the multi-GPU counterpart.
+    """
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    m_loc, n = c_local.shape
+    if rows is None:
+        t = torch.tensor([m_loc], dtype=torch.int64, device=c_local.device)
+        allr = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allr, t, group=group)
+        rows = [int(x.item()) for x in allr]
+    assert rows[rank] == m_loc, f"rank {rank}: {m_loc} rows, expected {rows[rank]}"
+    g_root = dist.get_global_rank(group, root) if group is not None else root
+    c_local = c_local.contiguous()
+    if rank != root:
+        if m_loc > 0:
+            for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, c_local, g_root, group)]):
+                w.wait()
+        return None
+    out = torch.empty((sum(rows), n), dtype=c_local.dtype, device=c_local.device)
+    offs = [sum(rows[:r]) for r in range(world)]
+    ops = []
+    for r in range(world):
+        if r == root or rows[r] == 0:
+            continue
+        g_r = dist.get_global_rank(group, r) if group is not None else r
+        ops.append(dist.P2POp(dist.irecv, out[offs[r]:offs[r] + rows[r]], g_r, group))
+    works = dist.batch_isend_irecv(ops) if ops else []
+    out[offs[root]:offs[root] + m_loc].copy_(c_local)
+    for w in works:
+        w.wait()
+    return out
+
+
 def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_splits: int = 3,
                        slice_dtype: torch.dtype = torch.float16, *, root: int = 0,
                        group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
-                       b_blocks: Optional[int] = None,
+                       b_blocks: Optional[int] = None, gather_to: Optional[int] = None,
                        backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B, A sharded by rows, B on ``root`` only.
 
@@ -176,6 +218,10 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
     slices as soon as it is split, so the broadcast of block c overlaps the
     split of block c + 1.  The blocks land in place in a column-blocked slice
     buffer that the GEMM reads directly (one launch over all of N).
+
+    ``gather_to=r``: rank r returns the whole C (M, N) instead (the row
+    blocks of every rank, in rank order, ``gather_rows``); the other ranks
+    still return their own rows.
     """
     backend = backend or Backend()
     dev = A_local.device
@@ -213,7 +259,14 @@ def ozaki_matmul_mrows(A_local: torch.Tensor, B: Optional[torch.Tensor], num_spl
         wk.wait()
     c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
                      skip_tail, b_block_cols=w)
-    return c.reshape(m_loc, n)
+    return _maybe_gather(c.reshape(m_loc, n), gather_to, group)
+
+
+def _maybe_gather(c_local: torch.Tensor, gather_to: Optional[int], group) -> torch.Tensor:
+    if gather_to is None:
+        return c_local
+    full = gather_rows(c_local, gather_to, group)
+    return full if full is not None else c_local
 
 
 def _all_gather_inplace(buf: torch.Tensor, rank: int, group, async_op: bool):
@@ -435,7 +488,7 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
 def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_splits: int = 3,
                          slice_dtype: torch.dtype = torch.float16, *, n: Optional[int] = None,
                          group=None, skip_tail: bool = False, residual: Optional[str] = "auto",
-                         transport: str = "auto",
+                         transport: str = "auto", gather_to: Optional[int] = None,
                          backend: Optional[Backend] = None) -> torch.Tensor:
     """C_local = A_local @ B with A sharded by rows and B by column panels.
 
@@ -459,6 +512,9 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
       arrived (on one of two streams), so the transfer overlaps the GEMMs.
       If the mappings cannot be set up on some rank, every rank uses the
       collective transport instead (``p2p_status`` reports why).
+
+    ``gather_to=r``: rank r returns the whole C (M, N) (``gather_rows``); the
+    other ranks still return their own rows.
     """
     backend = backend or Backend()
     dev = A_local.device
@@ -490,7 +546,7 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
         c = _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode, n, w,
                          ld, skip_tail, group)
         if c is not None:
-            return c.reshape(m_loc, n)
+            return _maybe_gather(c.reshape(m_loc, n), gather_to, group)
     # one block per rank (blocks past ceil(n / w) stay empty and are not read)
     b_sl, b_sc = _blocked_buffers(world, num_splits, w, ld, slice_dtype, dev)
     _split_block(backend, B_local, k, num_splits, alpha, slice_dtype, mode, b_sl[0, rank],
@@ -504,7 +560,7 @@ def ozaki_matmul_sharded(A_local: torch.Tensor, B_local: torch.Tensor, num_split
         wk.wait()
     c = backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, n, k, num_splits, A_local.dtype,
                      skip_tail, b_block_cols=w)
-    return c.reshape(m_loc, n)
+    return _maybe_gather(c.reshape(m_loc, n), gather_to, group)
 
 
 def ozaki_matmul_batches(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,

@@ -296,3 +296,44 @@ def test_weighted_rows_partition():
                 rows = ozd.weighted_rows(m, world, 0, disc)
                 assert sum(rows) == m and min(rows) >= 0 and len(rows) == world
     assert ozd.weighted_rows(8192, 8, 0, 768)[0] < 8192 // 8
+
+
+def case_gather(rank, world, out_dir):
+    """C gathered to a root: ragged row blocks (an empty one on the last
+    rank), both layouts, root 1; the other ranks keep their own rows."""
+    g = torch.Generator().manual_seed(12)
+    A = law(g, (41, 64))
+    B = law(g, (64, 300))
+    rows = [20, 21, 0][:world]
+    lo = sum(rows[:rank])
+    hi = lo + rows[rank]
+    c0, c1 = ozd.column_panel(300, world, rank)
+    c = ozd.ozaki_matmul_sharded(A[lo:hi], B[:, c0:c1], 4, torch.int8, gather_to=1,
+                                 backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"s{rank}.npy"), c.numpy())
+    d = ozd.ozaki_matmul_mrows(A[lo:hi], B if rank == 0 else None, 4, torch.int8, gather_to=1,
+                               backend=OracleBackend())
+    np.save(os.path.join(out_dir, f"m{rank}.npy"), d.numpy())
+    # the helper alone, with the row counts given
+    e = ozd.gather_rows(torch.full((rows[rank], 3), float(rank)), root=0, rows=rows)
+    if rank == 0:
+        np.save(os.path.join(out_dir, "e.npy"), e.numpy())
+    else:
+        assert e is None
+
+
+def test_gather_to_root_three_ranks(tmp_path):
+    codes = run_ranks(case_gather, 3, tmp_path)
+    assert codes == [0, 0, 0], [open(p).read() for p in tmp_path.glob("err*.txt")]
+    g = torch.Generator().manual_seed(12)
+    A = law(g, (41, 64))
+    B = law(g, (64, 300))
+    want = oracle.ozaki_matmul(A.numpy(), B.numpy(), 4, "int8", "fp64")
+    rows = [20, 21, 0]
+    for tag in ("s", "m"):
+        assert np.array_equal(np.load(tmp_path / f"{tag}1.npy"), want), tag
+        for r in (0, 2):
+            lo = sum(rows[:r])
+            assert np.array_equal(np.load(tmp_path / f"{tag}{r}.npy"), want[lo:lo + rows[r]])
+    e = np.load(tmp_path / "e.npy")
+    assert e.shape == (41, 3) and (e[:20] == 0).all() and (e[20:] == 1).all()

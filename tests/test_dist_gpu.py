@@ -1,6 +1,7 @@
 """Sharded paths on >= 2 GPUs with NCCL (one process per GPU): the
 M-row-sharded GEMM with the B broadcast, rows x column panels with the
-all-gather, and batch sharding give the same bits as the single-GPU call.
+all-gather or copy-engine pulls, the gather of C to one rank, and batch
+sharding give the same bits as the single-GPU call.
 Skipped with fewer than two GPUs."""
 
 import os
@@ -56,6 +57,15 @@ def _worker(rank, world, port, out_dir):
                 cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4,
                                               torch.int8, transport=transport)
                 ok1 = ok1 and torch.equal(cs, want_n)
+            # C gathered to rank 1: the whole product there, own rows elsewhere
+            full_n = oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4, torch.int8)
+            for transport in ("collective", "p2p"):
+                cg = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4,
+                                              torch.int8, transport=transport, gather_to=1)
+                ok1 = ok1 and torch.equal(cg, full_n if rank == 1 else want_n)
+            cm = ozd.ozaki_matmul_mrows(A[lo:hi].to(dev), Bn.to(dev) if rank == 0 else None, 4,
+                                        torch.int8, gather_to=1)
+            ok1 = ok1 and torch.equal(cm, full_n if rank == 1 else want_n)
         ozd.release_peer_buffers()
         A4 = torch.randn(4, 1, 64, 96, generator=g, dtype=torch.float64)
         B4 = torch.randn(1, 3, 96, 40, generator=g, dtype=torch.float64)
