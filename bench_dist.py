@@ -210,7 +210,7 @@ def run_rows(args, rank, world, dev):
     for _ in range(args.warmup):
         step()
     be.record = True
-    with bench.ClockSampler(local) as clk:
+    with bench.ClockSampler(local_index(dev)) as clk:
         launches0 = ozd._lib.load().oz_launch_count()
         ms = _timed(step, args.steps, stream)
         launches = ozd._lib.load().oz_launch_count() - launches0
@@ -224,7 +224,7 @@ def run_rows(args, rank, world, dev):
 
     # the other layout, and the gather of C to rank 0, in the same run
     alt = {}
-    n_alt = max(1, args.alt_steps)
+    n_alt = args.alt_steps
     if world > 1 and n_alt > 0:
         for name, (kind, transport, gather) in {
                 "gathered_to_rank0": (main_kind, args.transport, True),
