@@ -203,6 +203,7 @@ struct LevelP {
 };
 
 constexpr float kMagicF = 12582912.0f;            // 1.5 * 2^23
+constexpr double kMagicD = 6755399441055744.0;    // 1.5 * 2^52
 
 // exact double(n) for any 32-bit n: 1.5 * 2^52 + n, minus 1.5 * 2^52
 __device__ __forceinline__ double int_to_double_exact(int n) {
@@ -239,10 +240,13 @@ template <int SK> __device__ __forceinline__ float slice_to_f32(typename SliceT<
 }
 
 // level on an fp64 residual; the next residual goes to rn_d (EXACT) or,
-// rounded to fp32 like the reference's residual buffer, to rn_f
-template <int SK, bool EXACT>
-__device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv_d, float scale,
-                                                            bool upd, double &rn_d, float &rn_f) {
+// rounded to fp32 like the reference's residual buffer, to rn_f.  CLAMP:
+// the line maximum reaches 127.25 * scale, so +128 may occur and is clamped
+// to 127 (otherwise no element can round to 128).
+template <int SK, bool EXACT, bool CLAMP>
+__device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv_d,
+                                                            double nscale, bool upd,
+                                                            double &rn_d, float &rn_f) {
   const double x = __dmul_rn(r, inv_d);
   double qd;
   typename QOut<SK>::type q;
@@ -250,11 +254,13 @@ __device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv
     // the reference's fp64 t = x +- 0.5 (rounded), then trunc(t) =
     // sign(x) * floor(|t|) with floor(|t|) from the magic add rounded toward
     // zero: fl_rz(|t| + 1.5 * 2^52) = 1.5 * 2^52 + floor(|t|), whose low word
-    // is floor(|t|) (no conversion instruction)
+    // is floor(|t|) (no conversion instruction; integer sign handling keeps
+    // the fp64 temporaries, two registers each, few)
     const double t = __dadd_rn(x, copysign(0.5, x));
-    const int qa = __double2loint(__dadd_rz(fabs(t), 6755399441055744.0));
+    const int qa = __double2loint(__dadd_rz(fabs(t), kMagicD));
     const int sgn = __double2hiint(x) >> 31;
-    const int n = clamp_i8((qa ^ sgn) - sgn);
+    int n = (qa ^ sgn) - sgn;
+    if constexpr (CLAMP) n = clamp_i8(n);
     q = (uint32_t)n;
     qd = int_to_double_exact(n);
   } else {
@@ -263,7 +269,7 @@ __device__ __forceinline__ typename QOut<SK>::type step_f64(double r, double inv
   }
   if (upd) {
     // q * scale is exact, so one fused rounding equals the reference's r - q*s
-    const double d = __fma_rn(-qd, (double)scale, r);
+    const double d = __fma_rn(qd, nscale, r);
     if constexpr (EXACT) rn_d = d;
     else rn_f = __double2float_rn(d);
   }
@@ -336,31 +342,35 @@ __device__ __forceinline__ typename QOut<SK>::type step_f32_rd(float &r, float i
 
 // Two int8 steps at once with the packed fp32 instructions of sm_100
 // (__fmul2/__fadd2/__ffma2: per component exactly the scalar operations
-// above, half the instructions).  EXACT_HALF / FMA_RESID select the fp64-
-// input (step_f32_exact) or fp32-input (step_f32_rd) arithmetic.
-template <bool BIG, bool EXACT_HALF>
-__device__ __forceinline__ void step2_i8(float2 &r, float inv2, float scale, bool upd,
+// above).  |x| + 0.5 is two scalar adds, whose operand takes the absolute
+// value for free; the sign goes back on with one bit operation per element.
+// EXACT_HALF selects the fp64-input (step_f32_exact) or fp32-input
+// (step_f32_rd) rounding of |x| + 0.5; both residual updates are one fused
+// r + q * (-scale): q * scale is exact, so this rounds once like r - q*s.
+// CLAMP as in step_f64.
+template <bool BIG, bool EXACT_HALF, bool CLAMP>
+__device__ __forceinline__ void step2_i8(float2 &r, float inv2, float2 nscale, bool upd,
                                          uint32_t &w0, uint32_t &w1) {
   float2 x = r;
   if constexpr (BIG) x = __fmul2_rn(x, make_float2(18446744073709551616.0f, 18446744073709551616.0f));
   x = __fmul2_rn(x, make_float2(inv2, inv2));
-  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
-  const float2 t = EXACT_HALF ? __fadd2_rz(a, make_float2(0.5f, 0.5f))
-                              : __fadd2_rn(a, make_float2(0.5f, 0.5f));
+  const float2 t = EXACT_HALF ? make_float2(__fadd_rz(fabsf(x.x), 0.5f), __fadd_rz(fabsf(x.y), 0.5f))
+                              : make_float2(__fadd_rn(fabsf(x.x), 0.5f), __fadd_rn(fabsf(x.y), 0.5f));
   const float2 f = __fadd2_rz(t, make_float2(kMagicF, kMagicF));
   const float2 qa = __fadd2_rn(f, make_float2(-kMagicF, -kMagicF));   // floor(t), exact
-  const float2 q = make_float2(fminf(copysignf(qa.x, x.x), 127.0f),
-                               fminf(copysignf(qa.y, x.y), 127.0f));
+  float2 q = make_float2(copysignf(qa.x, x.x), copysignf(qa.y, x.y));
+  if constexpr (CLAMP) q = make_float2(fminf(q.x, 127.0f), fminf(q.y, 127.0f));
   const float2 m = __fadd2_rn(q, make_float2(kMagicF, kMagicF));
   w0 = __float_as_uint(m.x);
   w1 = __float_as_uint(m.y);
-  if (upd) {
-    if constexpr (EXACT_HALF) {
-      r = __ffma2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale), r);   // exact
-    } else {
-      r = __fadd2_rn(r, __fmul2_rn(make_float2(-q.x, -q.y), make_float2(scale, scale)));
-    }
-  }
+  if (upd) r = __ffma2_rn(q, nscale, r);
+}
+
+// max(|a|, |b|, |c|) in one instruction (three-input max of sm_100)
+__device__ __forceinline__ float max_abs3(float a, float b, float c) {
+  float d;
+  asm("max.abs.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // bulk (non-tensor) TMA copy global -> shared, completion counted on `bar`
@@ -409,43 +419,56 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
       } else {
         m = 0.f;
 #pragma unroll
-        for (int i = 0; i < NV; ++i) m = fmaxf(m, fabsf(vf(i)));
+        for (int i = 0; i + 1 < NV; i += 2) m = max_abs3(m, vf(i), vf(i + 1));
+        if constexpr (NV % 2 == 1) m = fmaxf(m, fabsf(vf(NV - 1)));
       }
       m = reduce(m, l);
       LevelP lv;
       lv.init(m, alpha);
       put_scale(l, lv.scale);
+      // int8: only a line whose maximum reaches 127.25 * scale (exact in
+      // fp32 for every int8 scale) can round an element to +128; the clamp
+      // is skipped on the others (fp64 maxima are rounded to fp32 at most
+      // 2^-24 below the true maximum, far from the 127.5 that rounds up)
+      const bool clamp = SK == OZ_I8 && m >= 127.25f * lv.scale;
       if (on_f64) {
         if constexpr (F64IN) {
           const double inv_d = lv.inv_d();
+          const double nscale = -(double)lv.scale;
+          auto level = [&](auto clamp_tag) {
+            constexpr bool C = decltype(clamp_tag)::value;
 #pragma unroll
-          for (int i = 0; i < NV; ++i) {
-            double nd = 0.0;
-            float nf = 0.f;
-            QT q = step_f64<SK, EXACT>(vd[i], inv_d, lv.scale, upd, nd, nf);
-            if constexpr (EXACT) vd[i] = nd;
-            else vf(i) = nf;
-            emit(l, i, q);
-          }
+            for (int i = 0; i < NV; ++i) {
+              double nd = 0.0;
+              float nf = 0.f;
+              QT q = step_f64<SK, EXACT, C>(vd[i], inv_d, nscale, upd, nd, nf);
+              if constexpr (EXACT) vd[i] = nd;
+              else vf(i) = nf;
+              emit(l, i, q);
+            }
+          };
+          if (clamp) level(std::true_type{});
+          else level(std::false_type{});
         }
       } else if constexpr (SK == OZ_I8 && NV % 2 == 0) {
         const float inv2 = lv.inv2();
+        const float2 nscale = make_float2(-lv.scale, -lv.scale);
+        auto level = [&](auto big_tag, auto clamp_tag) {
+          constexpr bool BIG = decltype(big_tag)::value, C = decltype(clamp_tag)::value;
+#pragma unroll
+          for (int i = 0; i < NV; i += 2) {
+            uint32_t w0, w1;
+            step2_i8<BIG, F64IN, C>(vf2[i >> 1], inv2, nscale, upd, w0, w1);
+            emit(l, i, w0);
+            emit(l, i + 1, w1);
+          }
+        };
         if (!lv.big()) {
-#pragma unroll
-          for (int i = 0; i < NV; i += 2) {
-            uint32_t w0, w1;
-            step2_i8<false, F64IN>(vf2[i >> 1], inv2, lv.scale, upd, w0, w1);
-            emit(l, i, w0);
-            emit(l, i + 1, w1);
-          }
+          if (clamp) level(std::false_type{}, std::true_type{});
+          else level(std::false_type{}, std::false_type{});
         } else {
-#pragma unroll
-          for (int i = 0; i < NV; i += 2) {
-            uint32_t w0, w1;
-            step2_i8<true, F64IN>(vf2[i >> 1], inv2, lv.scale, upd, w0, w1);
-            emit(l, i, w0);
-            emit(l, i + 1, w1);
-          }
+          if (clamp) level(std::true_type{}, std::true_type{});
+          else level(std::true_type{}, std::false_type{});
         }
       } else if (!lv.big()) {
         const float inv2 = lv.inv2();
@@ -656,20 +679,28 @@ __global__ void __launch_bounds__(CTA, kRowCTA / CTA)
 // ---------------------------------------------------------------------------
 // fp64 column pairs: the columns of a row-major B without a transposed copy
 // ---------------------------------------------------------------------------
-// Persistent kernel, one panel of 2 adjacent columns (lines) per iteration,
-// 512 threads per line as in split_rows_tma.  The panel's K rows arrive by
-// 2-D TMA boxes of 2 columns x 256 rows (16 bytes per row, zero-filled past
-// N and K) in chunks of 2048 rows -- one ring stage per chunk -- so no
-// transposed fp64 copy of B is written and read back.  Thread t holds rows
-// c*2048 + t + 512*e (e < 4) of chunk c: lane-consecutive rows, so the
-// shared-memory reads of one column are 2-way conflicted at most.  The two
-// columns are split one after the other from registers; each level's slice
-// row is assembled in shared memory (one byte / element per thread) and
-// written out with 16-byte stores.
+// Persistent kernel, one panel of 2 adjacent columns (lines) per iteration.
+// The panel's K rows arrive by 2-D TMA boxes of 2 columns x 256 rows (16
+// bytes per row, zero-filled past N and K) in chunks of 2048 rows -- one
+// ring stage per chunk -- so no transposed fp64 copy of B is written and
+// read back.  Each half of the CTA (256 threads) splits one column of the
+// panel, so the two columns' levels run side by side with a barrier domain
+// each (named barriers 1 and 2; barrier 0 only joins the halves once per
+// panel, when the ring stages are handed back).  Thread t of a half holds
+// rows c*2048 + t + 256*e (e < 8) of chunk c: lane-consecutive rows, so the
+// shared-memory reads of one column are 2-way conflicted at most.  Each
+// level's slice row is assembled in shared memory and written out with
+// 16-byte stores.
 constexpr int kPairRows = 2048;                 // rows per chunk (= ring stage)
 constexpr int kPairStage = kPairRows * 16;      // 32 KB
 constexpr int kPairMaxStages = 6;
 constexpr int kPairSmem = 224 * 1024;
+constexpr int kPairHalf = kRowCTA / 2;          // threads per column
+
+// barrier over the 256 threads of one half of the CTA (ids 1 and 2)
+__device__ __forceinline__ void half_sync(int half) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(kPairHalf) : "memory");
+}
 
 template <int SK, int NCH, bool EXACT>
 __global__ void __launch_bounds__(kRowCTA, 1)
@@ -679,13 +710,14 @@ __global__ void __launch_bounds__(kRowCTA, 1)
                        int NS) {
   using ST = typename SliceT<SK>::type;
   using QT = typename QOut<SK>::type;
-  constexpr int T = kRowCTA, VEC = 4, NV = NCH * VEC;
+  constexpr int T = kPairHalf, VEC = 8, NV = NCH * VEC;
   constexpr int OROW = NCH * kPairRows;         // slice row capacity (>= ld)
   extern __shared__ __align__(128) unsigned char smem[];
-  ST *obuf = reinterpret_cast<ST *>(smem + NS * kPairStage);                  // [2][OROW]
-  uint64_t *full = reinterpret_cast<uint64_t *>(obuf + 2 * OROW);
-  float *red = reinterpret_cast<float *>(full + kPairMaxStages);             // [2][16]
-  const int tl = threadIdx.x;
+  const int half = threadIdx.x / T, tl = threadIdx.x % T;
+  ST *obuf = reinterpret_cast<ST *>(smem + NS * kPairStage) + half * 2 * OROW;   // [2][OROW]
+  uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<ST *>(smem + NS * kPairStage) +
+                                                4 * OROW);
+  float *red = reinterpret_cast<float *>(full + kPairMaxStages) + half * 16;   // [2][8]
 
   // chunk q (running index over this CTA's chunks) lives in ring slot q % NS
   auto issue = [&](int64_t panel, int c, int slot) {
@@ -714,64 +746,54 @@ __global__ void __launch_bounds__(kRowCTA, 1)
   for (int64_t pi = 0; pi < my_panels; ++pi) {
     const int64_t panel = blockIdx.x + pi * gridDim.x;
     const int b = (int)(panel / ppb), n0 = (int)(panel % ppb) * 2;
-    auto load_col = [&](LineLevels<double, SK, NV, EXACT> &ll, int col, bool wait) {
+    const int line = n0 + half;
+    LineLevels<double, SK, NV, EXACT> ll;
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        const int64_t qc = q + c;
-        const int slot = (int)(qc % NS);
-        if (wait)
-          mbar_wait_bounded(&full[slot], (uint32_t)((qc / NS) & 1), (volatile int *)&abort_flag,
-                            DEV_TIMEOUT_PRODUCER);
-        const double *src = reinterpret_cast<const double *>(smem + slot * kPairStage) + col;
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t qc = q + c;
+      const int slot = (int)(qc % NS);
+      mbar_wait_bounded(&full[slot], (uint32_t)((qc / NS) & 1), (volatile int *)&abort_flag,
+                        DEV_TIMEOUT_PRODUCER);
+      const double *src = reinterpret_cast<const double *>(smem + slot * kPairStage) + half;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) ll.set(c * VEC + e, src[2 * (tl + e * T)]);
-      }
-    };
-    auto reduce = [&](float m, int l) -> float {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if ((threadIdx.x & 31) == 0) red[(l & 1) * 16 + (threadIdx.x >> 5)] = m;
-      __syncthreads();
-      const int lane = threadIdx.x & 31;
-      float v = lane < T / 32 ? red[(l & 1) * 16 + lane] : 0.f;
-#pragma unroll
-      for (int o = T / 64; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      return __shfl_sync(0xffffffffu, v, 0);
-    };
-    auto split_line = [&](LineLevels<double, SK, NV, EXACT> &ll, int line) {
-      const int64_t row0 = ((int64_t)b * s * lines + line) * (int64_t)ld;
-      auto put_scale = [&](int l, float sc) {
-        if (tl == 0) scales[((int64_t)b * s + l) * lines + line] = sc;
-      };
-      // element i = c*VEC + e is row c*2048 + tl + 512*e; rows past K hold
-      // zero (TMA fill), so the padding of the slice row is written as zero
-      auto emit = [&](int l, int i, QT qv) {
-        obuf[(l & 1) * OROW + (i / VEC) * kPairRows + tl + (i % VEC) * T] = to_slice<SK>(qv);
-      };
-      auto end_level = [&](int l) {
-        __syncthreads();
-        const unsigned char *src = reinterpret_cast<const unsigned char *>(obuf + (l & 1) * OROW);
-        unsigned char *dst = reinterpret_cast<unsigned char *>(out + row0 + (int64_t)l * lines * ld);
-        for (int o = tl * 16; o < ld_bytes; o += T * 16)
-          *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
-      };
-      ll.run(s, alpha, reduce, emit, put_scale, end_level);
-    };
-    {
-      LineLevels<double, SK, NV, EXACT> l0;
-      load_col(l0, 0, true);
-      split_line(l0, n0);
+      for (int e = 0; e < VEC; ++e) ll.set(c * VEC + e, src[2 * (tl + e * T)]);
     }
-    LineLevels<double, SK, NV, EXACT> l1;
-    load_col(l1, 1, false);
-    __syncthreads();                     // the panel's stages consumed by every thread
+    __syncthreads();                     // the panel's stages consumed by both halves
     if (threadIdx.x == 0)
       for (int c = 0; c < NCH; ++c) {
         const int64_t qn = q + c + NS;
         if (qn < my_chunks) issue(chunk_panel(qn), (int)(qn % NCH), (int)((q + c) % NS));
       }
     q += NCH;
-    if (n0 + 1 < lines) split_line(l1, n0 + 1);
+    if (line >= lines) continue;         // odd N: the last panel's second column
+    auto reduce = [&](float m, int l) -> float {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if ((tl & 31) == 0) red[(l & 1) * 8 + (tl >> 5)] = m;
+      half_sync(half);
+      const int lane = tl & 31;
+      float v = lane < T / 32 ? red[(l & 1) * 8 + lane] : 0.f;
+#pragma unroll
+      for (int o = T / 64; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      return __shfl_sync(0xffffffffu, v, 0);
+    };
+    const int64_t row0 = ((int64_t)b * s * lines + line) * (int64_t)ld;
+    auto put_scale = [&](int l, float sc) {
+      if (tl == 0) scales[((int64_t)b * s + l) * lines + line] = sc;
+    };
+    // element i = c*VEC + e is row c*2048 + tl + 256*e; rows past K hold
+    // zero (TMA fill), so the padding of the slice row is written as zero
+    auto emit = [&](int l, int i, QT qv) {
+      obuf[(l & 1) * OROW + (i / VEC) * kPairRows + tl + (i % VEC) * T] = to_slice<SK>(qv);
+    };
+    auto end_level = [&](int l) {
+      half_sync(half);
+      const unsigned char *src = reinterpret_cast<const unsigned char *>(obuf + (l & 1) * OROW);
+      unsigned char *dst = reinterpret_cast<unsigned char *>(out + row0 + (int64_t)l * lines * ld);
+      for (int o = tl * 16; o < ld_bytes; o += T * 16)
+        *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
+    };
+    ll.run(s, alpha, reduce, emit, put_scale, end_level);
   }
 }
 
@@ -1255,7 +1277,7 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
     return OZ_OK;
   const int nch0 = (std::max(K, ld) + kPairRows - 1) / kPairRows;
   const int nch = nch0 <= 1 ? 1 : nch0 <= 2 ? 2 : 4;
-  const int obuf = 2 * nch * kPairRows * (int)sizeof(ST);
+  const int obuf = 4 * nch * kPairRows * (int)sizeof(ST);    // [2 halves][2 levels]
   const int NS = std::min(kPairMaxStages, (kPairSmem - obuf - 1024) / kPairStage);
   if (NS < nch) return OZ_OK;                    // a panel's chunks must fit the ring
   auto enc = split_encode_fn();
