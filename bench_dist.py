@@ -348,7 +348,7 @@ def run_batches(args, rank, world, dev):
         ms = _timed(step, args.steps, stream)
         launches = ozd._lib.load().oz_launch_count() - launches0
     # self-check: each rank compares a sample of its first and last output
-    # batches with the oracle (fp16 slices: fp32 tensor-core sums, 1e-6)
+    # batches with the oracle (fp16 slices: fp32 tensor-core sums)
     c, start, stop = out["c"]
     torch.cuda.synchronize()
     rows, cols = _sample_lines(M, 12), _sample_lines(N, 12)
@@ -364,6 +364,7 @@ def run_batches(args, rank, world, dev):
         worst = max(worst, float(np.linalg.norm(got - want) / np.linalg.norm(want)))
         ex = a_s @ b_s
         rel = max(rel, float(np.linalg.norm(got - ex) / np.linalg.norm(ex)))
+    tol = max(1e-6, 2.5e-7 * math.sqrt(K))
     flags = torch.tensor([worst, rel], dtype=torch.float64, device=dev)
     dist.all_reduce(flags, op=dist.ReduceOp.MAX)
     if rank != 0:
@@ -379,8 +380,11 @@ def run_batches(args, rank, world, dev):
                                   "GPUs; each rank splits only the A and B members its range "
                                   "uses; no exchange",
                    "l2": "no flush: operands larger than the 126 MB L2"},
-        "parity_checked": bool(flags[0].item() < 1e-6),
-        "vs_oracle": "rel diff < 1e-6 on 12x12 samples of every rank's first and last batch",
+        "parity_checked": bool(flags[0].item() < tol),
+        "vs_oracle": (f"rel diff < {tol:.2g} (the fp16 tensor cores sum each pair product "
+                      "over K in fp32; the oracle rounds the exact product once: "
+                      "max(1e-6, 2.5e-7 sqrt(K)), as in tests/test_configs_gpu.py) on 12x12 "
+                      "samples of every rank's first and last batch"),
         "max_diff_vs_oracle": float(flags[0].item()),
         "rel_err_vs_fp64_sample": float(flags[1].item()),
         "clocks": clk.summary(), "gpu_launches": launches, "e2e": None,
