@@ -387,17 +387,20 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // streaming kernels.  NV values per thread; `emit(l, idx, q)` stores slice
 // element idx of level l; `reduce(m, l)` returns the line max over the
 // threads of the line.
-template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
+// REG64 = false: an fp64 line whose level 0 the caller runs itself (from
+// shared memory, split_rows_f64s): no fp64 registers, levels from `first`.
+template <typename TIn, int SK, int NV, bool EXACT, bool REG64 = true> struct LineLevels {
   using ST = typename SliceT<SK>::type;
   using QT = typename QOut<SK>::type;
   static constexpr bool F64IN = sizeof(TIn) == 8;
-  double vd[F64IN ? NV : 1];
+  static_assert(REG64 || (F64IN && !EXACT), "only fp64 lines with an fp32 residual drop vd");
+  double vd[F64IN && REG64 ? NV : 1];
   // fp32 values as register pairs (the packed f32x2 steps take both halves)
   float2 vf2[(NV + 1) / 2];
   __device__ __forceinline__ float &vf(int i) { return (i & 1) ? vf2[i >> 1].y : vf2[i >> 1].x; }
 
   __device__ __forceinline__ void set(int i, TIn v) {
-    if constexpr (F64IN) vd[i] = v;
+    if constexpr (F64IN && REG64) vd[i] = v;
     else vf(i) = InTraits<TIn>::to_float(v);
   }
 
@@ -406,15 +409,17 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
   // runs once per level on every thread, after all of that level's emits.
   template <typename Reduce, typename Emit, typename Scale, typename EndLevel>
   __device__ __forceinline__ void run(int s, int alpha, Reduce reduce, Emit emit, Scale put_scale,
-                                      EndLevel end_level) {
-    for (int l = 0; l < s; ++l) {
+                                      EndLevel end_level, int first = 0) {
+    for (int l = first; l < s; ++l) {
       const bool upd = l < s - 1;
-      const bool on_f64 = F64IN && (EXACT || l == 0);
+      const bool on_f64 = REG64 && F64IN && (EXACT || l == 0);
       float m;
       if (on_f64) {
         double md = 0.0;
+        if constexpr (REG64) {
 #pragma unroll
-        for (int i = 0; i < NV; ++i) md = fmax(md, fabs(vd[i]));
+          for (int i = 0; i < NV; ++i) md = fmax(md, fabs(vd[i]));
+        }
         m = __double2float_rn(md);
       } else {
         m = 0.f;
@@ -432,7 +437,7 @@ template <typename TIn, int SK, int NV, bool EXACT> struct LineLevels {
       // 2^-24 below the true maximum, far from the 127.5 that rounds up)
       const bool clamp = SK == OZ_I8 && m >= 127.25f * lv.scale;
       if (on_f64) {
-        if constexpr (F64IN) {
+        if constexpr (F64IN && REG64) {
           const double inv_d = lv.inv_d();
           const double nscale = -(double)lv.scale;
           auto level = [&](auto clamp_tag) {
@@ -677,6 +682,149 @@ __global__ void __launch_bounds__(CTA, kRowCTA / CTA)
 }
 
 // ---------------------------------------------------------------------------
+// fp64 rows with an fp32 residual: level 0 straight from shared memory
+// ---------------------------------------------------------------------------
+// Three 256-thread CTAs per SM, one row each.  Level 0 reads the row's fp64
+// values from the ring stage twice (maximum, then quantisation into the fp32
+// residual, which stays in registers); the stage is then handed back to the
+// next row's bulk copy while levels 1.. run from registers.  No fp64 value
+// is held in registers, so three rows fit per SM instead of two, with three
+// barrier domains.  Same element mapping, arithmetic and stores as
+// split_rows_tma (thread tl holds elements [(c*T + tl)*4, +4), c < NCH).
+constexpr int kRowsSCTA = 256;
+constexpr int kRowsSPerSM = 3;
+
+template <int SK, int NCH>
+__global__ void __launch_bounds__(kRowsSCTA, kRowsSPerSM)
+    split_rows_f64s(const double *__restrict__ in, int64_t stride_b, int64_t stride_line,
+                    int lines, int64_t total, int K, int ld, int s, int alpha,
+                    typename SliceT<SK>::type *__restrict__ out, float *__restrict__ scales,
+                    int rowp) {
+  using ST = typename SliceT<SK>::type;
+  using QT = typename QOut<SK>::type;
+  constexpr int T = kRowsSCTA, VEC = 4, NV = NCH * VEC;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + rowp);
+  float *red = reinterpret_cast<float *>(full + 1);   // [2][8]
+  const int tl = threadIdx.x;
+  const uint32_t row_bytes = (uint32_t)K * 8u;
+  const bool one_batch = total == lines;
+  auto issue = [&](int64_t row) {
+    int64_t b, line;
+    row_coords(row, lines, one_batch, b, line);
+    mbar_arrive_expect_tx(full, row_bytes);
+    bulk_load(smem, in + b * stride_b + line * stride_line, row_bytes, full);
+  };
+  if (tl == 0) {
+    mbar_init(full, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tl == 0 && blockIdx.x < total) issue(blockIdx.x);
+
+  // which chunks lie inside the row pitch (written), wholly inside K (read
+  // as a vector) or straddle K (read element by element); fixed per thread
+  uint32_t in_ld = 0, in_k = 0, part_k = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int k0 = (c * T + tl) * VEC;
+    in_ld |= (uint32_t)(k0 < ld) << c;
+    in_k |= (uint32_t)(k0 + VEC <= K) << c;
+    part_k |= (uint32_t)(k0 < K && k0 + VEC > K) << c;
+  }
+  const double *srow = reinterpret_cast<const double *>(smem) + tl * VEC;
+  auto chunk = [&](int c) -> Pack<double, VEC> {
+    Pack<double, VEC> pk;
+    if ((in_k >> c) & 1) {
+      pk = *reinterpret_cast<const Pack<double, VEC> *>(srow + c * T * VEC);
+    } else {
+      const int k0 = (c * T + tl) * VEC;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        pk.e[e] = (((part_k >> c) & 1) && k0 + e < K) ? srow[c * T * VEC + e] : 0.0;
+    }
+    return pk;
+  };
+  // consecutive reductions alternate between two slots (also across rows,
+  // where no other barrier separates one row's last level from the next
+  // row's first): a slot is rewritten only after the barrier of the
+  // reduction in between, which every thread passes after reading it
+  int nred = 0;
+  auto reduce = [&](float m, int) -> float {
+    const int slot = (nred++ & 1) * 8;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tl & 31) == 0) red[slot + (tl >> 5)] = m;
+    __syncthreads();
+    const int lane = tl & 31;
+    float v = lane < T / 32 ? red[slot + lane] : 0.f;
+#pragma unroll
+    for (int o = T / 64; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return __shfl_sync(0xffffffffu, v, 0);
+  };
+
+  volatile int abort_flag = 0;
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < total; row += gridDim.x, ++it) {
+    mbar_wait_bounded(full, it & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_PRODUCER);
+    int64_t b, line;
+    row_coords(row, lines, one_batch, b, line);
+    ST *dst = out + (b * s * lines + line) * (int64_t)ld + tl * VEC;
+    const int64_t level_stride = (int64_t)lines * ld;
+    QT pq[VEC];
+    ST *dl = dst;
+    auto put_scale = [&](int l, float sc) {
+      if (tl == 0) scales[(b * s + l) * lines + line] = sc;
+      dl = dst + l * level_stride;
+    };
+    auto emit = [&](int l, int i, QT q) {
+      (void)l;
+      pq[i % VEC] = q;
+      if (i % VEC == VEC - 1) {
+        const int c = i / VEC;
+        if ((in_ld >> c) & 1) store_slices<SK, VEC>(dl + c * T * VEC, pq);
+      }
+    };
+    LineLevels<double, SK, NV, false, false> ll;
+    // level 0 from shared memory: the maximum, then the quantisation
+    double md = 0.0;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const Pack<double, VEC> pk = chunk(c);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) md = fmax(md, fabs(pk.e[e]));
+    }
+    const float m = reduce(__double2float_rn(md), 0);
+    LevelP lv;
+    lv.init(m, alpha);
+    put_scale(0, lv.scale);
+    const bool upd = s > 1;
+    const double inv_d = lv.inv_d();
+    const double nscale = -(double)lv.scale;
+    auto level0 = [&](auto clamp_tag) {
+      constexpr bool C = decltype(clamp_tag)::value;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const Pack<double, VEC> pk = chunk(c);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          double nd = 0.0;
+          float nf = 0.f;
+          const QT q = step_f64<SK, false, C>(pk.e[e], inv_d, nscale, upd, nd, nf);
+          ll.vf(c * VEC + e) = nf;
+          emit(0, c * VEC + e, q);
+        }
+      }
+    };
+    if (SK == OZ_I8 && m >= 127.25f * lv.scale) level0(std::true_type{});
+    else level0(std::false_type{});
+    __syncthreads();                     // the stage is read by every thread
+    if (tl == 0 && row + gridDim.x < total) issue(row + gridDim.x);
+    ll.run(s, alpha, reduce, emit, put_scale, [](int) {}, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // fp64 column pairs: the columns of a row-major B without a transposed copy
 // ---------------------------------------------------------------------------
 // Persistent kernel, one panel of 2 adjacent columns (lines) per iteration.
@@ -688,9 +836,10 @@ __global__ void __launch_bounds__(CTA, kRowCTA / CTA)
 // each (named barriers 1 and 2; barrier 0 only joins the halves once per
 // panel, when the ring stages are handed back).  Thread t of a half holds
 // rows c*2048 + t + 256*e (e < 8) of chunk c: lane-consecutive rows, so the
-// shared-memory reads of one column are 2-way conflicted at most.  Each
-// level's slice row is assembled in shared memory and written out with
-// 16-byte stores.
+// shared-memory reads of one column are 2-way conflicted at most, and each
+// store of a warp writes 32 consecutive slice elements of the K-contiguous
+// slice row (rows past K are zero from the TMA fill, which writes the row's
+// padding).
 constexpr int kPairRows = 2048;                 // rows per chunk (= ring stage)
 constexpr int kPairStage = kPairRows * 16;      // 32 KB
 constexpr int kPairMaxStages = 6;
@@ -702,7 +851,10 @@ __device__ __forceinline__ void half_sync(int half) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(kPairHalf) : "memory");
 }
 
-template <int SK, int NCH, bool EXACT>
+// FULL: the slice row is exactly the chunks' length (ld == NCH * 2048), so
+// no store needs a bound (a per-element bound keeps a predicate per element
+// live through the levels).
+template <int SK, int NCH, bool EXACT, bool FULL>
 __global__ void __launch_bounds__(kRowCTA, 1)
     split_colpairs_tma(const __grid_constant__ CUtensorMap tm_in, int lines, int64_t panels,
                        int ppb, int K, int ld, int s, int alpha,
@@ -711,12 +863,10 @@ __global__ void __launch_bounds__(kRowCTA, 1)
   using ST = typename SliceT<SK>::type;
   using QT = typename QOut<SK>::type;
   constexpr int T = kPairHalf, VEC = 8, NV = NCH * VEC;
-  constexpr int OROW = NCH * kPairRows;         // slice row capacity (>= ld)
+  static_assert(NV <= 32, "one bit per element in the store mask");
   extern __shared__ __align__(128) unsigned char smem[];
   const int half = threadIdx.x / T, tl = threadIdx.x % T;
-  ST *obuf = reinterpret_cast<ST *>(smem + NS * kPairStage) + half * 2 * OROW;   // [2][OROW]
-  uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<ST *>(smem + NS * kPairStage) +
-                                                4 * OROW);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + NS * kPairStage);
   float *red = reinterpret_cast<float *>(full + kPairMaxStages) + half * 16;   // [2][8]
 
   // chunk q (running index over this CTA's chunks) lives in ring slot q % NS
@@ -740,9 +890,15 @@ __global__ void __launch_bounds__(kRowCTA, 1)
   if (threadIdx.x == 0)
     for (int64_t q = 0; q < NS && q < my_chunks; ++q) issue(chunk_panel(q), (int)(q % NCH), (int)q);
 
+  // element i = c*VEC + e is slice element k = c*2048 + tl + 256*e; bit i
+  // set when k lies inside the slice row (k < ld)
+  uint32_t in_ld = 0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+    in_ld |= (uint32_t)((i / VEC) * kPairRows + tl + (i % VEC) * T < ld) << i;
+
   volatile int abort_flag = 0;
   int64_t q = 0;
-  const int ld_bytes = ld * (int)sizeof(ST);
   for (int64_t pi = 0; pi < my_panels; ++pi) {
     const int64_t panel = blockIdx.x + pi * gridDim.x;
     const int b = (int)(panel / ppb), n0 = (int)(panel % ppb) * 2;
@@ -766,6 +922,9 @@ __global__ void __launch_bounds__(kRowCTA, 1)
       }
     q += NCH;
     if (line >= lines) continue;         // odd N: the last panel's second column
+    // consecutive reductions alternate between two slots; a slot is
+    // rewritten only after the barrier of the reduction in between (and the
+    // panels are separated by the barrier above)
     auto reduce = [&](float m, int l) -> float {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -777,23 +936,16 @@ __global__ void __launch_bounds__(kRowCTA, 1)
       for (int o = T / 64; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
       return __shfl_sync(0xffffffffu, v, 0);
     };
-    const int64_t row0 = ((int64_t)b * s * lines + line) * (int64_t)ld;
+    ST *row0 = out + ((int64_t)b * s * lines + line) * (int64_t)ld + tl;
+    ST *dl = row0;
     auto put_scale = [&](int l, float sc) {
       if (tl == 0) scales[((int64_t)b * s + l) * lines + line] = sc;
+      dl = row0 + (int64_t)l * lines * ld;
     };
-    // element i = c*VEC + e is row c*2048 + tl + 256*e; rows past K hold
-    // zero (TMA fill), so the padding of the slice row is written as zero
-    auto emit = [&](int l, int i, QT qv) {
-      obuf[(l & 1) * OROW + (i / VEC) * kPairRows + tl + (i % VEC) * T] = to_slice<SK>(qv);
+    auto emit = [&](int, int i, QT qv) {
+      if (FULL || ((in_ld >> i) & 1)) dl[(i / VEC) * kPairRows + (i % VEC) * T] = to_slice<SK>(qv);
     };
-    auto end_level = [&](int l) {
-      half_sync(half);
-      const unsigned char *src = reinterpret_cast<const unsigned char *>(obuf + (l & 1) * OROW);
-      unsigned char *dst = reinterpret_cast<unsigned char *>(out + row0 + (int64_t)l * lines * ld);
-      for (int o = tl * 16; o < ld_bytes; o += T * 16)
-        *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
-    };
-    ll.run(s, alpha, reduce, emit, put_scale, end_level);
+    ll.run(s, alpha, reduce, emit, put_scale, [](int) {});
   }
 }
 
@@ -1132,6 +1284,46 @@ bool rows_two_ctas_resident() {
   return ok;
 }
 
+// fp64 rows, fp32 residual, up to 8192 elements: split_rows_f64s when three
+// of its CTAs are resident on one SM (asked once per instance).
+template <int SK>
+bool rows_f64s_resident(int smem) {
+  static int blocks = -1;
+  if (blocks < 0) {
+    auto kern = split_rows_f64s<SK, 8>;
+    const int max_smem = 64 * 1024 + 256;
+    int b = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, kRowsSCTA, max_smem) !=
+            cudaSuccess) {
+      (void)cudaGetLastError();
+      b = 0;
+    }
+    blocks = b;
+  }
+  return smem <= 64 * 1024 + 256 && blocks >= kRowsSPerSM;
+}
+
+template <int SK>
+int launch_rows_f64s(const double *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K,
+                     int ld, int s, int alpha, void *slices, float *scales, cudaStream_t st,
+                     int rowp) {
+  using ST = typename SliceT<SK>::type;
+  auto kern = split_rows_f64s<SK, 8>;
+  const int smem = rowp + 8 + 2 * 8 * 4;
+  if (int rc = check_cuda(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          "cudaFuncSetAttribute(split_rows_f64s)"))
+    return rc;
+  const int64_t total = batch * (int64_t)lines;
+  const int grid = (int)std::min<int64_t>(total, (int64_t)sm_count_split() * kRowsSPerSM);
+  count_launch();
+  kern<<<grid, kRowsSCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
+                                       reinterpret_cast<ST *>(slices), scales, rowp);
+  return check_cuda(cudaGetLastError(), "split_rows_f64s launch");
+}
+
 template <typename TIn, int SK, bool EXACT>
 int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines, int K, int ld,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
@@ -1175,6 +1367,16 @@ int launch_rows(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lines,
     // 512-thread CTA per SM runs instead.
     const char *env = getenv("OZ_SPLIT_ROWS_CTA");
     const bool two = !(env && atoi(env) == 512);
+    // default: level 0 from shared memory, three rows per SM (fp32 residual,
+    // rows longer than 4096 elements); OZ_SPLIT_ROWS_CTA=256 or 512 (read on
+    // every call) selects the register-resident kernels
+    if constexpr (!EXACT) {
+      if (!env && c512 > 2 && c512 <= 4 && rows_f64s_resident<SK>(rowp + 8 + 2 * 8 * 4)) {
+        *done = true;
+        return launch_rows_f64s<SK>(in, sb, sl, batch, lines, K, ld, s, alpha, slices, scales,
+                                    st, rowp);
+      }
+    }
     if (two && c512 <= 4) {
       const int NS = std::min(kRowMaxStages, (kRowSmem / 2) / rowp);
       if (NS >= 1 && rows_two_ctas_resident<TIn, SK, EXACT>()) {
@@ -1277,8 +1479,7 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
     return OZ_OK;
   const int nch0 = (std::max(K, ld) + kPairRows - 1) / kPairRows;
   const int nch = nch0 <= 1 ? 1 : nch0 <= 2 ? 2 : 4;
-  const int obuf = 4 * nch * kPairRows * (int)sizeof(ST);    // [2 halves][2 levels]
-  const int NS = std::min(kPairMaxStages, (kPairSmem - obuf - 1024) / kPairStage);
+  const int NS = std::min(kPairMaxStages, (kPairSmem - 1024) / kPairStage);
   if (NS < nch) return OZ_OK;                    // a panel's chunks must fit the ring
   auto enc = split_encode_fn();
   if (!enc) return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1294,7 +1495,7 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
     return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled (column pairs) failed (%d)", (int)r);
   const int ppb = (lines + 1) / 2;
   const int64_t panels = (int64_t)ppb * batch;
-  const int smem = NS * kPairStage + obuf + kPairMaxStages * 8 + 2 * 16 * 4;
+  const int smem = NS * kPairStage + kPairMaxStages * 8 + 2 * 16 * 4;
   const int grid = (int)std::min<int64_t>(panels, (int64_t)sm_count_split());
   ST *o = reinterpret_cast<ST *>(slices);
   auto go = [&](auto kern) -> int {
@@ -1307,9 +1508,12 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
     *done = true;
     return check_cuda(cudaGetLastError(), "split_colpairs_tma launch");
   };
-  if (nch <= 1) return go(split_colpairs_tma<SK, 1, EXACT>);
-  if (nch <= 2) return go(split_colpairs_tma<SK, 2, EXACT>);
-  return go(split_colpairs_tma<SK, 4, EXACT>);
+  const bool full = ld == nch * kPairRows;
+  if (nch <= 1)
+    return full ? go(split_colpairs_tma<SK, 1, EXACT, true>) : go(split_colpairs_tma<SK, 1, EXACT, false>);
+  if (nch <= 2)
+    return full ? go(split_colpairs_tma<SK, 2, EXACT, true>) : go(split_colpairs_tma<SK, 2, EXACT, false>);
+  return full ? go(split_colpairs_tma<SK, 4, EXACT, true>) : go(split_colpairs_tma<SK, 4, EXACT, false>);
 }
 
 template <typename TIn, int SK, bool EXACT>

@@ -57,15 +57,20 @@ def test_split_matches_reference_golden(case):
                      want if sk == "int8" else want.astype(np.float64))
 
 
-@pytest.mark.parametrize("cta", ["256", "512"])
+@pytest.mark.parametrize("cta", ["default", "256", "512"])
 @pytest.mark.parametrize("name", ["rows_f64_i8_s4_k8192", "cols_f64_i8_s2_k4100"])
 def test_split_fp64_row_kernel_both_cta_shapes(name, cta, monkeypatch):
-    """fp64 rows of up to 8192 elements run on two 256-thread CTAs per SM by
-    default, or on one 512-thread CTA (OZ_SPLIT_ROWS_CTA=512, read on every
-    call; the same kernel is the fallback when two CTAs are not resident).
-    Both are bit-exact on the K = 8192 and K = 4100 goldens, presented as
-    contiguous rows."""
-    monkeypatch.setenv("OZ_SPLIT_ROWS_CTA", cta)
+    """fp64 rows of 4097..8192 elements with an fp32 residual run by default
+    on three 256-thread CTAs per SM that take level 0 from shared memory
+    (split_rows_f64s); OZ_SPLIT_ROWS_CTA (read on every call) selects the
+    register-resident kernels instead: two 256-thread CTAs per SM (256) or
+    one 512-thread CTA (512, also the fallback when fewer CTAs are
+    resident).  All are bit-exact on the K = 8192 and K = 4100 goldens,
+    presented as contiguous rows."""
+    if cta == "default":
+        monkeypatch.delenv("OZ_SPLIT_ROWS_CTA", raising=False)
+    else:
+        monkeypatch.setenv("OZ_SPLIT_ROWS_CTA", cta)
     case = next(c for c in SPLITS if c["name"] == name)
     x = case["x"] if case["layout"] == "rows" else np.swapaxes(case["x"], -1, -2)
     xd = to_dev(np.ascontiguousarray(x), "fp64")
