@@ -90,7 +90,14 @@ def slice_row_elems(k: int, slice_dtype: torch.dtype) -> int:
     return ((k * es + 127) // 128 * 128) // es if k > 0 else 0
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(device: torch.device) -> int:
+    """The current CUDA stream of ``device`` as an address (the raw accessor
+    when torch has it: a tenth of the host time of building a Stream object)."""
+    if _RAW_STREAM is not None and device.index is not None:
+        return _RAW_STREAM(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -283,47 +290,94 @@ def ozaki_matmul(A: torch.Tensor, B: torch.Tensor, num_splits: int = 3,
     assert K == K2, f"contraction dim mismatch: A K={K}, B K={K2}"
     _check_cuda(A, B)
 
+    key = (A.dtype, slice_dtype, num_splits, A.shape, A.stride(), B.shape, B.stride(),
+           residual, bool(skip_tail), A.device)
+    plan = _PLANS.get(key)
+    if plan is None:
+        plan = _matmul_plan(A, B, num_splits, slice_dtype, residual, skip_tail)
+        if len(_PLANS) >= 256:
+            _PLANS.clear()
+        _PLANS[key] = plan
+    if verbose and plan.log_line is not None:
+        print(plan.log_line)
+    if plan.empty:
+        return torch.empty(plan.out_shape, dtype=A.dtype, device=A.device)
+    # each distinct batch member is split once (no broadcast copies); one
+    # library call splits B by columns and A by rows into the workspace and
+    # runs the fused cross-GEMM
+    if plan.flat:
+        a_ptr, b_ptr = A.data_ptr(), B.data_ptr()
+        a_st, b_st = plan.a_strides, plan.b_strides
+    else:
+        A3 = A.reshape(plan.a_batches, plan.m, plan.k)
+        B3 = B.reshape(plan.b_batches, plan.k, plan.n)
+        a_ptr, b_ptr = A3.data_ptr(), B3.data_ptr()
+        a_st, b_st = A3.stride(), B3.stride()
+    ws = torch.empty(plan.ws_alloc, dtype=torch.uint8, device=A.device)
+    C = torch.empty(plan.c_shape, dtype=A.dtype, device=A.device)
+    _lib.check(plan.lib.oz_matmul(
+        a_ptr, b_ptr, plan.code, plan.bn, plan.a_batches, plan.b_batches, plan.a_idx, plan.b_idx,
+        plan.m, plan.n, plan.k, a_st[0], a_st[1], a_st[2], b_st[0], b_st[1], b_st[2],
+        num_splits, plan.scode, plan.mode, C.data_ptr(), plan.n, plan.flags,
+        ws.data_ptr(), plan.ws_bytes, _stream_ptr(A.device)))
+    return C.view(plan.out_shape)
+
+
+class _MatmulPlan:
+    """What ``ozaki_matmul`` derives from the operands' dtypes, shapes and
+    strides alone (alpha, the batch index arrays, the workspace size, the
+    output shape), kept per distinct call signature so that a repeated small
+    product pays only for its allocations and one library call."""
+    __slots__ = ("empty", "out_shape", "log_line", "flat", "a_strides", "b_strides", "a_batches",
+                 "b_batches", "m", "n", "k", "bn", "code", "scode", "mode", "flags", "ws_bytes",
+                 "ws_alloc", "c_shape", "a_idx", "b_idx", "a_idx_t", "b_idx_t", "lib")
+
+
+_PLANS = {}
+
+
+def _matmul_plan(A, B, num_splits, slice_dtype, residual, skip_tail) -> _MatmulPlan:
+    p = _MatmulPlan()
     input_dtype = A.dtype
+    M, K = A.shape[-2:]
+    N = B.shape[-1]
     dot_accum_dtype = select_dot_accum_dtype(slice_dtype)
     a_batch, b_batch = tuple(A.shape[:-2]), tuple(B.shape[:-2])
     batch_shape = broadcast_batch(a_batch, b_batch)
     BN = math.prod(batch_shape)
-    out_shape = (*batch_shape, M, N)
-    if BN == 0:
-        return torch.empty(out_shape, dtype=input_dtype, device=A.device)
-
+    p.out_shape = (*batch_shape, M, N)
+    p.log_line = None
+    p.empty = BN == 0
+    if p.empty:
+        return p
     alpha = compute_split_bits(K, slice_dtype=slice_dtype, dot_accum_dtype=dot_accum_dtype)
-    if verbose:
-        print(f"[Ozaki] batch={batch_shape}, M={M}, K={K}, N={N}, "
-              f"input={input_dtype}, slice={slice_dtype}, "
-              f"dot_accum={dot_accum_dtype}, out_accum={select_out_accum_dtype(input_dtype)}, "
-              f"splits={num_splits}, alpha={alpha}")
-
-    if M == 0 or N == 0:
-        return torch.empty(out_shape, dtype=input_dtype, device=A.device)
-    mode = _residual_mode(residual, num_splits, input_dtype)
-    # each distinct batch member is split once (no broadcast copies); one
-    # library call splits B by columns and A by rows into the workspace and
-    # runs the fused cross-GEMM
-    A3 = A.reshape(math.prod(a_batch), M, K)
-    B3 = B.reshape(math.prod(b_batch), K, N)
-    a_idx = _batch_index(a_batch, batch_shape, A.device)
-    b_idx = _batch_index(b_batch, batch_shape, A.device)
-    lib = _lib.load()
-    code, scode = _OZ_DTYPE[input_dtype], _OZ_DTYPE[slice_dtype]
-    ws_bytes = lib.oz_matmul_workspace_bytes(code, A3.shape[0], B3.shape[0], M, N, K,
-                                             A3.stride(1), A3.stride(2), B3.stride(1),
-                                             B3.stride(2), num_splits, scode)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
-    C = torch.empty((BN, M, N), dtype=input_dtype, device=A.device)
-    _lib.check(lib.oz_matmul(
-        A3.data_ptr(), B3.data_ptr(), code, BN, A3.shape[0], B3.shape[0],
-        a_idx.data_ptr() if a_idx is not None else None,
-        b_idx.data_ptr() if b_idx is not None else None, M, N, K,
-        A3.stride(0), A3.stride(1), A3.stride(2), B3.stride(0), B3.stride(1), B3.stride(2),
-        num_splits, scode, mode, C.data_ptr(), N, _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0,
-        ws.data_ptr(), ws_bytes, _stream_ptr(A.device)))
-    return C.view(out_shape)
+    p.log_line = (f"[Ozaki] batch={batch_shape}, M={M}, K={K}, N={N}, "
+                  f"input={input_dtype}, slice={slice_dtype}, "
+                  f"dot_accum={dot_accum_dtype}, out_accum={select_out_accum_dtype(input_dtype)}, "
+                  f"splits={num_splits}, alpha={alpha}")
+    p.empty = M == 0 or N == 0
+    if p.empty:
+        return p
+    p.m, p.n, p.k, p.bn = M, N, K, BN
+    p.mode = _residual_mode(residual, num_splits, input_dtype)
+    p.a_batches, p.b_batches = math.prod(a_batch), math.prod(b_batch)
+    p.flat = A.dim() == 2 and B.dim() == 2
+    A3 = A.reshape(p.a_batches, M, K)
+    B3 = B.reshape(p.b_batches, K, N)
+    p.a_strides, p.b_strides = A3.stride(), B3.stride()
+    p.a_idx_t = _batch_index(a_batch, batch_shape, A.device)
+    p.b_idx_t = _batch_index(b_batch, batch_shape, A.device)
+    p.a_idx = p.a_idx_t.data_ptr() if p.a_idx_t is not None else None
+    p.b_idx = p.b_idx_t.data_ptr() if p.b_idx_t is not None else None
+    p.lib = _lib.load()
+    p.code, p.scode = _OZ_DTYPE[input_dtype], _OZ_DTYPE[slice_dtype]
+    p.flags = _lib.OZ_GEMM_SKIP_TAIL if skip_tail else 0
+    p.ws_bytes = p.lib.oz_matmul_workspace_bytes(p.code, p.a_batches, p.b_batches, M, N, K,
+                                                 p.a_strides[1], p.a_strides[2], p.b_strides[1],
+                                                 p.b_strides[2], num_splits, p.scode)
+    p.ws_alloc = max(p.ws_bytes, 1)
+    p.c_shape = (BN, M, N)
+    return p
 
 
 _STREAMS = {}

@@ -9,6 +9,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <unordered_map>
+
 #include "../../include/ozaki_b200.h"
 
 namespace oz {
@@ -21,6 +24,31 @@ int check_cuda(cudaError_t e, const char *what);
 // Kernel launches issued by the library (oz_launch_count), counted at each
 // launch site.
 void count_launch();
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for a kernel, issued only
+// when this device has not yet allowed the kernel that much shared memory
+// (the attribute is an upper bound, so a larger earlier value covers smaller
+// launches).  Saves a driver call per launch on small, launch-bound products.
+inline int set_smem_once(const void *kern, int smem, const char *what) {
+  constexpr int kDevs = 64;
+  static std::mutex mu;
+  static std::unordered_map<const void *, int> allowed[kDevs];
+  int dev = -1;
+  const bool cached = cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kDevs;
+  if (cached) {
+    std::lock_guard<std::mutex> lk(mu);
+    const auto it = allowed[dev].find(kern);
+    if (it != allowed[dev].end() && it->second >= smem) return 0;
+  }
+  const int rc =
+      check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), what);
+  if (rc == 0 && cached) {
+    std::lock_guard<std::mutex> lk(mu);
+    int &v = allowed[dev][kern];
+    if (v < smem) v = smem;
+  }
+  return rc;
+}
 
 // Device-side status word of this translation unit: kernels write a nonzero
 // code here when a bounded wait gives up.  Each .cu file exposes it through a

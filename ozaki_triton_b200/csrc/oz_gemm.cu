@@ -488,9 +488,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &
   auto kern = cross_gemm_kernel<KIND, OUTK, NT, PAIR>;
   const int smem = p.stages * stage_bytes(p.s, NT, PAIR) + 1024 + kBarrierBytes +
                    scale_stage_bytes(p.s, NT);
-  if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               smem),
-                          "cudaFuncSetAttribute(cross_gemm)"))
+  if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(cross_gemm)"))
     return rc;
   const int units = min(p.num_tiles, sm_count() / PAIR);
   cudaLaunchConfig_t cfg = {};

@@ -18,6 +18,9 @@
 // reciprocal (same correctly rounded result).
 //
 // Kernels:
+//   split_rows_f64s    : fp64 rows of 4097..8192 elements with the fp32
+//                        residual: three CTAs per SM, level 0 read from
+//                        shared memory, later levels from registers.
 //   split_rows_tma     : the split axis is contiguous (rows of A, or rows of a
 //                        transposed workspace).  512 threads own a line;
 //                        whole lines arrive by bulk TMA copies.
@@ -694,7 +697,9 @@ __global__ void __launch_bounds__(CTA, kRowCTA / CTA)
 constexpr int kRowsSCTA = 256;
 constexpr int kRowsSPerSM = 3;
 
-template <int SK, int NCH>
+// FULL: the row holds exactly NCH * T * 4 elements and so does its slice row
+// (K = ld = 8192 with NCH = 8), so no chunk needs a bound check.
+template <int SK, int NCH, bool FULL>
 __global__ void __launch_bounds__(kRowsSCTA, kRowsSPerSM)
     split_rows_f64s(const double *__restrict__ in, int64_t stride_b, int64_t stride_line,
                     int lines, int64_t total, int K, int ld, int s, int alpha,
@@ -735,7 +740,7 @@ __global__ void __launch_bounds__(kRowsSCTA, kRowsSPerSM)
   const double *srow = reinterpret_cast<const double *>(smem) + tl * VEC;
   auto chunk = [&](int c) -> Pack<double, VEC> {
     Pack<double, VEC> pk;
-    if ((in_k >> c) & 1) {
+    if (FULL || ((in_k >> c) & 1)) {
       pk = *reinterpret_cast<const Pack<double, VEC> *>(srow + c * T * VEC);
     } else {
       const int k0 = (c * T + tl) * VEC;
@@ -782,7 +787,7 @@ __global__ void __launch_bounds__(kRowsSCTA, kRowsSPerSM)
       pq[i % VEC] = q;
       if (i % VEC == VEC - 1) {
         const int c = i / VEC;
-        if ((in_ld >> c) & 1) store_slices<SK, VEC>(dl + c * T * VEC, pq);
+        if (FULL || ((in_ld >> c) & 1)) store_slices<SK, VEC>(dl + c * T * VEC, pq);
       }
     };
     LineLevels<double, SK, NV, false, false> ll;
@@ -1249,9 +1254,7 @@ int launch_rows_nc(const TIn *in, int64_t sb, int64_t sl, int64_t batch, int lin
   using ST = typename SliceT<SK>::type;
   auto kern = split_rows_tma<TIn, SK, T, NC, EXACT, CTA>;
   const int smem = NS * (CTA / T) * rowp + kRowMaxStages * 8 + 2 * 16 * 4;
-  if (int rc = check_cuda(
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          "cudaFuncSetAttribute(split_rows)"))
+  if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(split_rows)"))
     return rc;
   const int64_t total = batch * (int64_t)lines;
   const int64_t groups = (total + (CTA / T) - 1) / (CTA / T);
@@ -1290,7 +1293,7 @@ template <int SK>
 bool rows_f64s_resident(int smem) {
   static int blocks = -1;
   if (blocks < 0) {
-    auto kern = split_rows_f64s<SK, 8>;
+    auto kern = split_rows_f64s<SK, 8, false>;
     const int max_smem = 64 * 1024 + 256;
     int b = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) !=
@@ -1310,18 +1313,19 @@ int launch_rows_f64s(const double *in, int64_t sb, int64_t sl, int64_t batch, in
                      int ld, int s, int alpha, void *slices, float *scales, cudaStream_t st,
                      int rowp) {
   using ST = typename SliceT<SK>::type;
-  auto kern = split_rows_f64s<SK, 8>;
   const int smem = rowp + 8 + 2 * 8 * 4;
-  if (int rc = check_cuda(
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          "cudaFuncSetAttribute(split_rows_f64s)"))
-    return rc;
   const int64_t total = batch * (int64_t)lines;
   const int grid = (int)std::min<int64_t>(total, (int64_t)sm_count_split() * kRowsSPerSM);
-  count_launch();
-  kern<<<grid, kRowsSCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
-                                       reinterpret_cast<ST *>(slices), scales, rowp);
-  return check_cuda(cudaGetLastError(), "split_rows_f64s launch");
+  auto go = [&](auto kern) -> int {
+    if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(split_rows_f64s)"))
+      return rc;
+    count_launch();
+    kern<<<grid, kRowsSCTA, smem, st>>>(in, sb, sl, lines, total, K, ld, s, alpha,
+                                         reinterpret_cast<ST *>(slices), scales, rowp);
+    return check_cuda(cudaGetLastError(), "split_rows_f64s launch");
+  };
+  if (K == 8 * kRowsSCTA * 4 && ld == K) return go(split_rows_f64s<SK, 8, true>);
+  return go(split_rows_f64s<SK, 8, false>);
 }
 
 template <typename TIn, int SK, bool EXACT>
@@ -1440,9 +1444,7 @@ int launch_cols_v(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int line
     return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled (split) failed (%d)", (int)r);
   const int smem = NS * STAGE + fixed;
   auto kern = split_cols_tma<TIn, SK, V, EXACT>;
-  if (int rc = check_cuda(
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          "cudaFuncSetAttribute(split_cols)"))
+  if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(split_cols)"))
     return rc;
   const int64_t work = (int64_t)((lines + W - 1) / W) * batch;
   const int clusters = (int)std::min<int64_t>(work, (int64_t)std::max(1, sm_count_split() / CL));
@@ -1499,9 +1501,7 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
   const int grid = (int)std::min<int64_t>(panels, (int64_t)sm_count_split());
   ST *o = reinterpret_cast<ST *>(slices);
   auto go = [&](auto kern) -> int {
-    if (int rc = check_cuda(
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-            "cudaFuncSetAttribute(split_colpairs)"))
+    if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(split_colpairs)"))
       return rc;
     count_launch();
     kern<<<grid, kRowCTA, smem, st>>>(map, lines, panels, ppb, K, ld, s, alpha, o, scales, NS);
