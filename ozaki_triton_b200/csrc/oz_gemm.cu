@@ -59,17 +59,19 @@ struct GemmParams {
   int gm;                // row tiles per raster group
   int bw, bblocks;       // B stored in column blocks of bw columns (bblocks per batch)
   int stages;            // pipeline depth
+  int pa;                // A slices per pass (1, or 2 when 2 * s * NT fits the 512 TMEM columns)
   uint32_t idesc;        // instruction descriptor without the N field
 };
 
-// One pipeline stage holds, for one 128-byte K block, the A tile of the pass
-// (128 rows of A_i) followed by the stacked B tiles of all s slices
-// (s x NT/PAIR rows: B_0 rows, B_1 rows, ...).  Stacking lets one MMA with
-// N = 256 cover several slices at once: its accumulator columns are the
-// products with consecutive B slices.
+// One pipeline stage holds, for one 128-byte K block, the A tiles of the
+// pass (128 rows of each of its pa A slices) followed by the stacked B tiles
+// of all s slices (s x NT/PAIR rows: B_0 rows, B_1 rows, ...).  Stacking lets
+// one MMA with N = 256 cover several slices at once: its accumulator columns
+// are the products with consecutive B slices.  Two A slices per pass (when
+// their 2 * s accumulators fit TMEM) double the MMA work per fed byte of B.
 __host__ __device__ constexpr int a_tile_bytes() { return kBM * kKBytes; }
-__host__ __device__ inline int stage_bytes(int s, int nt, int pair) {
-  return a_tile_bytes() + s * (nt / pair) * kKBytes;
+__host__ __device__ inline int stage_bytes(int s, int nt, int pair, int pa) {
+  return pa * a_tile_bytes() + s * (nt / pair) * kKBytes;
 }
 
 // B scales of a tile staged for the epilogue: two tiles x s slices x NT floats.
@@ -148,7 +150,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int s = p.s;
   const int S = p.stages;
-  const int sbytes = stage_bytes(s, NT, PAIR);
+  const int PA = p.pa;
+  const int sbytes = stage_bytes(s, NT, PAIR, PA);
+  const int bofs = PA * a_tile_bytes();          // B stack offset inside a stage
+  const int pcols = PA * s * NT;                  // TMEM columns of one pass
 
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -165,9 +170,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int nbuf = (2 * s * NT <= 512) ? 2 : 1;
+  const int nbuf = (2 * pcols <= 512) ? 2 : 1;
   int tcols = 32;
-  while (tcols < nbuf * s * NT) tcols <<= 1;
+  while (tcols < nbuf * pcols) tcols <<= 1;
   const uint32_t rank = (PAIR == 2) ? cluster_ctarank() : 0;
   const bool leader = rank == 0;
   const int unit = blockIdx.x / PAIR;          // this CTA's pair (or CTA) index
@@ -223,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int blk = (nb * NT) / p.bw;
         const int brow = nb * NT - blk * p.bw + (int)rank * R;
         const int bz = (bi * p.bblocks + blk) * s;
-        for (int i = 0; ok && i < s; ++i) {
+        for (int i = 0; ok && i < s; i += PA) {
           for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
             const int slot = it % S;
             if (!(ok = mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, abort_flag,
@@ -233,12 +238,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if constexpr (PAIR == 2) {
               if (leader) mbar_arrive_expect_tx(&full[slot], tx);
               const uint32_t fb = leader_addr(&full[slot]);
-              tma_load_3d_pair(st, &tm_a, fb, kb * kKBytes, arow, ai * s + i);
-              tma_load_3d_pair(st + a_tile_bytes(), &tm_b, fb, kb * kKBytes, brow, bz);
+              tma_load_3d_pair(st, &tm_a, fb, kb * kKBytes, arow, ai * s + i);   // PA slices
+              tma_load_3d_pair(st + bofs, &tm_b, fb, kb * kKBytes, brow, bz);
             } else {
               mbar_arrive_expect_tx(&full[slot], tx);
-              tma_load_3d(st, &tm_a, &full[slot], kb * kKBytes, arow, ai * s + i);
-              tma_load_3d(st + a_tile_bytes(), &tm_b, &full[slot], kb * kKBytes, brow, bz);
+              tma_load_3d(st, &tm_a, &full[slot], kb * kKBytes, arow, ai * s + i);   // PA slices
+              tma_load_3d(st + bofs, &tm_b, &full[slot], kb * kKBytes, brow, bz);
             }
           }
         }
@@ -264,37 +269,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       };
       for (int t = unit; ok && t < p.num_tiles; t += units) {
-        for (int i = 0; ok && i < s; ++i, ++pass) {
-          const int js = p.skip_tail ? s - i : s;
-          const int groups = (js + SPG - 1) / SPG;
+        for (int i = 0; ok && i < s; i += PA, ++pass) {
           const int buf = pass % nbuf;
           const uint32_t use = pass / nbuf;
           if (!(ok = mbar_wait_bounded(&acc_empty[buf], (use & 1) ^ 1, abort_flag,
                                        DEV_TIMEOUT_MMA)))
             break;
           tc_fence_after();
-          const uint32_t d0 = tmem_base + (uint32_t)(buf * s * NT);
+          const uint32_t d0 = tmem_base + (uint32_t)(buf * pcols);
           for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
             const int slot = it % S;
             if (!(ok = mbar_wait_bounded(&full[slot], (it / S) & 1, abort_flag, DEV_TIMEOUT_MMA)))
               break;
             const uint32_t sa = base + slot * sbytes;
-            const uint64_t adesc = smem_desc_sw128(sa);
 #pragma unroll 1
-            for (int g = 0; g < groups; ++g) {
-              const int sg = min(SPG, js - g * SPG);
-              const uint32_t idesc = p.idesc | ((uint32_t)((sg * NT) >> 3) << 17);
-              const uint64_t bdesc =
-                  smem_desc_sw128(sa + a_tile_bytes() + g * (256 / PAIR) * kKBytes);
+            for (int a = 0; a < PA; ++a) {
+              // A slice i + a: its accumulators follow those of slice i
+              const int js = p.skip_tail ? s - (i + a) : s;
+              const int groups = (js + SPG - 1) / SPG;
+              const uint64_t adesc = smem_desc_sw128(sa + a * a_tile_bytes());
+              const uint32_t da = d0 + (uint32_t)(a * s * NT);
+#pragma unroll 1
+              for (int g = 0; g < groups; ++g) {
+                const int sg = min(SPG, js - g * SPG);
+                const uint32_t idesc = p.idesc | ((uint32_t)((sg * NT) >> 3) << 17);
+                const uint64_t bdesc = smem_desc_sw128(sa + bofs + g * (256 / PAIR) * kKBytes);
 #pragma unroll
-              for (int kk = 0; kk < kKBytes / 32; ++kk) {
-                // advance 32 bytes along K inside the 128-byte swizzle row
-                if constexpr (PAIR == 2)
-                  tc_mma_pair<KIND>(d0 + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
-                                    bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
-                else
-                  tc_mma<KIND>(d0 + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
-                               bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                for (int kk = 0; kk < kKBytes / 32; ++kk) {
+                  // advance 32 bytes along K inside the 128-byte swizzle row
+                  if constexpr (PAIR == 2)
+                    tc_mma_pair<KIND>(da + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
+                                      bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                  else
+                    tc_mma<KIND>(da + (uint32_t)(g * 256), adesc + (uint64_t)(kk * 2),
+                                 bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                }
               }
             }
             release(&empty[slot]);
@@ -351,39 +360,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              DEV_TIMEOUT_EPILOGUE);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      for (int i = 0; i < s; ++i, ++pass) {
-        const int js = p.skip_tail ? s - i : s;
+      for (int i = 0; i < s; i += PA, ++pass) {
         const int buf = pass % nbuf;
         const uint32_t use = pass / nbuf;
-        const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + i) * p.m + m] : 0.f;
         // every lane waits, then the warp agrees (tcgen05.ld needs a converged warp)
         ok = mbar_wait_bounded(&acc_full[buf], use & 1, abort_flag, DEV_TIMEOUT_EPILOGUE);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        for (int j = 0; j < js; ++j) {
-          const float *sbj = sbt + j * NT + half * NH;
-          const int g = j / SPG, jj = j % SPG;
-          int col;
-          if constexpr (PAIR == 2) {
-            const int rg = min(SPG, js - g * SPG) * NH;    // columns per CTA half in group
-            col = buf * s * NT + g * 256 + half * rg + jj * NH;
-          } else {
-            col = buf * s * NT + g * 256 + jj * NT + half * NH;
-          }
+        // A slices i, i + 1, .. of the pass in order, each with its B slices
+        // in order: the reference's i-major, j-minor sum
+        for (int a = 0; a < PA; ++a) {
+          const int ia = i + a;
+          const int js = p.skip_tail ? s - ia : s;
+          const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + ia) * p.m + m] : 0.f;
+          for (int j = 0; j < js; ++j) {
+            const float *sbj = sbt + j * NT + half * NH;
+            const int g = j / SPG, jj = j % SPG;
+            int col;
+            if constexpr (PAIR == 2) {
+              const int rg = min(SPG, js - g * SPG) * NH;    // columns per CTA half in group
+              col = buf * pcols + a * s * NT + g * 256 + half * rg + jj * NH;
+            } else {
+              col = buf * pcols + a * s * NT + g * 256 + jj * NT + half * NH;
+            }
 #pragma unroll
-          for (int c = 0; c < NH / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld16_at(lane_addr + (uint32_t)(col + c * 16), r);
-            tmem_ld_wait16(r);
+            for (int c = 0; c < NH / 16; ++c) {
+              uint32_t r[16];
+              tmem_ld16_at(lane_addr + (uint32_t)(col + c * 16), r);
+              tmem_ld_wait16(r);
 #pragma unroll
-            for (int x = 0; x < 16; ++x) {
-              const float sb = sbj[c * 16 + x];
-              float v;
-              if constexpr (KIND == 0) v = __int2float_rn((int)r[x]);
-              else v = __uint_as_float(r[x]);
-              v = __fmul_rn(__fmul_rn(v, sa), sb);
-              out[c * 16 + x] = acc_add<ACC>(out[c * 16 + x], v);
+              for (int x = 0; x < 16; ++x) {
+                const float sb = sbj[c * 16 + x];
+                float v;
+                if constexpr (KIND == 0) v = __int2float_rn((int)r[x]);
+                else v = __uint_as_float(r[x]);
+                v = __fmul_rn(__fmul_rn(v, sa), sb);
+                out[c * 16 + x] = acc_add<ACC>(out[c * 16 + x], v);
+              }
             }
           }
         }
@@ -486,7 +500,7 @@ template <int KIND, int OUTK, int NT, int PAIR>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
                 cudaStream_t st) {
   auto kern = cross_gemm_kernel<KIND, OUTK, NT, PAIR>;
-  const int smem = p.stages * stage_bytes(p.s, NT, PAIR) + 1024 + kBarrierBytes +
+  const int smem = p.stages * stage_bytes(p.s, NT, PAIR, p.pa) + 1024 + kBarrierBytes +
                    scale_stage_bytes(p.s, NT);
   if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(cross_gemm)"))
     return rc;
@@ -637,9 +651,16 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
   const TileChoice tc = choose_tile(kind, num_splits, batch, m, n, k);
   const int nt = tc.nt, pair = tc.pair;
+  // two A slices per pass when num_splits is even and both slices'
+  // accumulators fit the 512 TMEM columns (s = 2 with 128-column tiles: the
+  // MMA work per fed byte of the pass doubles); OZ_GEMM_PA=1 turns it off
+  int pa = (num_splits % 2 == 0 && 2 * num_splits * nt <= 512) ? 2 : 1;
+  if (const char *env = getenv("OZ_GEMM_PA"))
+    if (atoi(env) == 1) pa = 1;
   CUtensorMap ta, tb;
+  // A: one box = the K block of the pass's pa consecutive slices
   if (int rc = make_map(&ta, a_slices, (uint64_t)ld_bytes, (uint64_t)m,
-                        (uint64_t)(a_batches * num_splits), kBM, 1))
+                        (uint64_t)(a_batches * num_splits), kBM, (uint32_t)pa))
     return rc;
   // B: one box = the K block of all num_splits slices, stacked
   // (column blocks: the slices of block c of batch b are matrices (b*blocks + c)*s + j)
@@ -670,8 +691,9 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
   p.idesc = make_idesc(slice_dtype, kBM * pair);
+  p.pa = pa;
   p.stages = min(kMaxStages, (kSmemBudget - scale_stage_bytes(num_splits, nt)) /
-                                 stage_bytes(num_splits, nt, pair));
+                                 stage_bytes(num_splits, nt, pair, pa));
   if (tc.stages > 0 && tc.stages < p.stages) p.stages = tc.stages;
 
   cudaEvent_t ev0 = g_prof_begin, ev1 = g_prof_end;

@@ -41,11 +41,12 @@ constexpr TileEntry kTileTable[] = {
     {0, 8, 1, 16384, 16384, 16384, 2, 64, 16, 0},      // 252.9 / 258.5 (1,64)
     // shards of C3 / C5 on 2-8 GPUs (rows of A x all of N, or x one column block)
     {0, 4, 1, 2048, 8192, 8192, 2, 128, 16, 0},        // 1.578 / 1.861 (1,128)
-    // the 8-GPU p2p blocks (1024 rows x 1024 columns) run eight at a time on
-    // their own streams: 0.835 ms for all eight with CTA pairs of 128 columns
-    // vs 0.926 ms with (1, 64) tiles, which are faster for one block alone
-    // (0.163 vs 0.170 ms); 1-GPU emulation of one rank's GEMM phase
-    {0, 4, 1, 1024, 1024, 8192, 2, 128, 16, 0},
+    // the 8-GPU p2p blocks (1024 rows x 1024 columns): one block alone 0.163 ms
+    // vs 0.170 (2,64).  A 1-GPU emulation of a rank's eight block GEMMs with all
+    // blocks present favoured (2,128) on one stream per block (0.835 vs 0.926
+    // ms), but on 8 GPUs, with blocks arriving one by one, that setting gave
+    // 1043 TFLOPS against 1107 for this entry with 2 GEMM streams
+    {0, 4, 1, 1024, 1024, 8192, 1, 64, 16, 0},
     {0, 4, 1, 2048, 16384, 16384, 2, 128, 16, 0},      // 6.73 / 8.32 (1,128)
 };
 

@@ -377,12 +377,12 @@ _PEER_CACHE: Dict[tuple, PeerBlocks] = {}
 # streams of the p2p transport: copy streams (blocks arrive one after another,
 # so the first block GEMMs start early) and streams the block GEMMs run on
 # (None = one per peer block, besides the current stream, which runs the GEMM
-# of the rank's own block).  One rank's GEMM phase at 8192^3 on 8 GPUs (eight
-# 1024 x 1024 blocks, CTA-pair tiles), emulated on one B200 with all blocks
-# present: 0.835 ms with a stream per block, 0.959 ms with 2 streams, 1.34 ms
-# with one; a single GEMM over all eight blocks takes 0.790 ms.
+# of the rank's own block).  Measured on 8 B200s at 8192^3: 1 copy stream and
+# 2 GEMM streams with the table's (1, 64) tiles for the 1024 x 1024 blocks:
+# 1107 TFLOPS; CTA-pair tiles on one stream per block: 1043 TFLOPS (although
+# a 1-GPU emulation with every block already present favoured them).
 P2P_COPY_STREAMS = 1
-P2P_GEMM_STREAMS: Optional[int] = None
+P2P_GEMM_STREAMS: Optional[int] = 2
 
 
 def p2p_status(group=None) -> str:

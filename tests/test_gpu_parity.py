@@ -266,13 +266,36 @@ def test_broadcast_batch_semantics():
     assert same_bits(host(c), want)
 
 
-def test_skip_tail_matches_oracle():
+@pytest.mark.parametrize("s", [2, 4])
+def test_skip_tail_matches_oracle(s):
+    """skip_tail drops the pairs i + j >= s; with s = 2 both A slices share a
+    pass (the second one with one B slice)."""
     rng = np.random.default_rng(6)
     a = rng.standard_normal((96, 256)); b = rng.standard_normal((256, 80))
-    c = oz.ozaki_matmul(to_dev(a, "fp64"), to_dev(b, "fp64"), num_splits=4,
+    c = oz.ozaki_matmul(to_dev(a, "fp64"), to_dev(b, "fp64"), num_splits=s,
                         slice_dtype=torch.int8, skip_tail=True)
-    want = oracle.ozaki_matmul(a, b, 4, "int8", "fp64", skip_tail=True)
+    want = oracle.ozaki_matmul(a, b, s, "int8", "fp64", skip_tail=True)
     assert same_bits(host(c), want)
+
+
+@pytest.mark.parametrize("sk,tile", [("int8", "2,128"), ("int8", "1,128"), ("fp16", "2,128"),
+                                     ("fp16", "1,64"), ("fp32", "2,128")])
+def test_two_a_slices_per_pass_bit_identical(sk, tile, monkeypatch):
+    """With an even num_splits whose accumulators fit TMEM twice (s = 2) a
+    GEMM pass covers two A slices; OZ_GEMM_PA=1 runs one per pass.  Both give
+    the same bits: the same MMAs per pair and the same epilogue order."""
+    rng = np.random.default_rng(78)
+    M, N, K = 333, 260, 1500
+    a = rng.standard_normal((M, K)); b = rng.standard_normal((K, N))
+    ad, bd = to_dev(a, "fp64"), to_dev(b, "fp64")
+    monkeypatch.setenv("OZ_GEMM_TILE", tile)
+    c2 = oz.ozaki_matmul(ad, bd, num_splits=2, slice_dtype=TDT[sk])
+    monkeypatch.setenv("OZ_GEMM_PA", "1")
+    c1 = oz.ozaki_matmul(ad, bd, num_splits=2, slice_dtype=TDT[sk])
+    assert torch.equal(c1.view(torch.int64), c2.view(torch.int64))
+    if sk == "int8":
+        assert same_bits(host(c2), oracle.ozaki_matmul(a, b, 2, "int8", "fp64"))
+    assert oz.device_status() == 0
 
 
 def test_error_paths():
