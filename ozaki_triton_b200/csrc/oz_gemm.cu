@@ -282,8 +282,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!(ok = mbar_wait_bounded(&full[slot], (it / S) & 1, abort_flag, DEV_TIMEOUT_MMA)))
               break;
             const uint32_t sa = base + slot * sbytes;
+            const int pc = min(PA, s - i);             // A slices in this pass
 #pragma unroll 1
-            for (int a = 0; a < PA; ++a) {
+            for (int a = 0; a < pc; ++a) {
               // A slice i + a: its accumulators follow those of slice i
               const int js = p.skip_tail ? s - (i + a) : s;
               const int groups = (js + SPG - 1) / SPG;
@@ -370,7 +371,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         // A slices i, i + 1, .. of the pass in order, each with its B slices
         // in order: the reference's i-major, j-minor sum
-        for (int a = 0; a < PA; ++a) {
+        const int pc = min(PA, s - i);
+        for (int a = 0; a < pc; ++a) {
           const int ia = i + a;
           const int js = p.skip_tail ? s - ia : s;
           const float sa = (m < p.m) ? p.a_scales[((int64_t)ai * s + ia) * p.m + m] : 0.f;
@@ -651,10 +653,16 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   const int kind = slice_dtype == OZ_I8 ? 0 : (slice_dtype == OZ_F32 ? 2 : 1);
   const TileChoice tc = choose_tile(kind, num_splits, batch, m, n, k);
   const int nt = tc.nt, pair = tc.pair;
-  // two A slices per pass when num_splits is even and both slices'
-  // accumulators fit the 512 TMEM columns (s = 2 with 128-column tiles: the
-  // MMA work per fed byte of the pass doubles); OZ_GEMM_PA=1 turns it off
-  int pa = (num_splits % 2 == 0 && 2 * num_splits * nt <= 512) ? 2 : 1;
+  // two A slices per pass when both slices' accumulators fit the 512 TMEM
+  // columns (s = 2 with 128-column tiles, s <= 4 with 64): the MMA work per
+  // fed byte of the pass doubles (C2: 0.63 -> 0.77 of peak; C3 with 64-column
+  // single-CTA tiles: 7.26 -> 5.98 ms), at the cost of the double-buffered
+  // accumulators when 4 * s * NT > 512.  With an odd num_splits the last pass
+  // has one slice; its A box still covers two matrices (the next one lies
+  // past the last slice: another batch member's first slice, or outside the
+  // tensor, which the copy fills with zeros) and is not multiplied.
+  // OZ_GEMM_PA=1 turns it off (benchmarking and tests).
+  int pa = (num_splits >= 2 && 2 * num_splits * nt <= 512) ? 2 : 1;
   if (const char *env = getenv("OZ_GEMM_PA"))
     if (atoi(env) == 1) pa = 1;
   CUtensorMap ta, tb;

@@ -42,10 +42,11 @@ constexpr TileEntry kTileTable[] = {
     // shards of C3 / C5 on 2-8 GPUs (rows of A x all of N, or x one column block)
     {0, 4, 1, 2048, 8192, 8192, 2, 128, 16, 0},        // 1.578 / 1.861 (1,128)
     // the 8-GPU p2p blocks (1024 rows x 1024 columns): one block alone 0.163 ms
-    // vs 0.170 (2,64).  A 1-GPU emulation of a rank's eight block GEMMs with all
-    // blocks present favoured (2,128) on one stream per block (0.835 vs 0.926
-    // ms), but on 8 GPUs, with blocks arriving one by one, that setting gave
-    // 1043 TFLOPS against 1107 for this entry with 2 GEMM streams
+    // vs 0.170 (2,64) with one A slice per pass (these 64-column tiles now
+    // take two per pass).  A 1-GPU emulation of a rank's eight block GEMMs with
+    // all blocks present favoured (2,128) on one stream per block (0.835 vs
+    // 0.926 ms), but on 8 GPUs, with blocks arriving one by one, that setting
+    // gave 1043 TFLOPS against 1107 for this entry with 2 GEMM streams
     {0, 4, 1, 1024, 1024, 8192, 1, 64, 16, 0},
     {0, 4, 1, 2048, 16384, 16384, 2, 128, 16, 0},      // 6.73 / 8.32 (1,128)
 };

@@ -278,23 +278,29 @@ def test_skip_tail_matches_oracle(s):
     assert same_bits(host(c), want)
 
 
-@pytest.mark.parametrize("sk,tile", [("int8", "2,128"), ("int8", "1,128"), ("fp16", "2,128"),
-                                     ("fp16", "1,64"), ("fp32", "2,128")])
-def test_two_a_slices_per_pass_bit_identical(sk, tile, monkeypatch):
-    """With an even num_splits whose accumulators fit TMEM twice (s = 2) a
-    GEMM pass covers two A slices; OZ_GEMM_PA=1 runs one per pass.  Both give
-    the same bits: the same MMAs per pair and the same epilogue order."""
-    rng = np.random.default_rng(78)
+@pytest.mark.parametrize("sk,tile,s,batch", [
+    ("int8", "2,128", 2, 1), ("int8", "1,128", 2, 1), ("fp16", "2,128", 2, 1),
+    ("fp16", "1,64", 2, 1), ("fp32", "2,128", 2, 1), ("int8", "2,64", 3, 1),
+    ("int8", "1,64", 3, 3), ("fp16", "2,64", 3, 2), ("int8", "1,64", 4, 1),
+    ("int8", "2,64", 4, 2)])
+def test_two_a_slices_per_pass_bit_identical(sk, tile, s, batch, monkeypatch):
+    """When two A slices' accumulators fit TMEM (s = 2 with 128-column tiles,
+    s <= 4 with 64) a GEMM pass covers two A slices; OZ_GEMM_PA=1 runs one per
+    pass.  Both give the same bits: the same MMAs per pair and the same
+    epilogue order.  With s = 3 the last pass has one slice, and its A box
+    reaches into the next batch member's slices (or past the last one)."""
+    rng = np.random.default_rng(78 + s + batch)
     M, N, K = 333, 260, 1500
-    a = rng.standard_normal((M, K)); b = rng.standard_normal((K, N))
+    a = rng.standard_normal((batch, M, K)); b = rng.standard_normal((K, N))
     ad, bd = to_dev(a, "fp64"), to_dev(b, "fp64")
     monkeypatch.setenv("OZ_GEMM_TILE", tile)
-    c2 = oz.ozaki_matmul(ad, bd, num_splits=2, slice_dtype=TDT[sk])
+    c2 = oz.ozaki_matmul(ad, bd, num_splits=s, slice_dtype=TDT[sk])
     monkeypatch.setenv("OZ_GEMM_PA", "1")
-    c1 = oz.ozaki_matmul(ad, bd, num_splits=2, slice_dtype=TDT[sk])
+    c1 = oz.ozaki_matmul(ad, bd, num_splits=s, slice_dtype=TDT[sk])
     assert torch.equal(c1.view(torch.int64), c2.view(torch.int64))
     if sk == "int8":
-        assert same_bits(host(c2), oracle.ozaki_matmul(a, b, 2, "int8", "fp64"))
+        for i in range(batch):
+            assert same_bits(host(c2[i]), oracle.ozaki_matmul(a[i], b, s, "int8", "fp64"))
     assert oz.device_status() == 0
 
 
