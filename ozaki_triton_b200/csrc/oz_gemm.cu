@@ -17,11 +17,13 @@
 //              tcgen05.ld of the int32/fp32 accumulators, scaling, fp64/fp32
 //              outer accumulation in registers, store of C.
 // Per output tile (128 rows x NT columns) the kernel runs one "pass" per A
-// slice i: a full K loop that accumulates the pair products A_i B_j for every
-// j into s TMEM accumulators of NT columns each (s * NT <= 512 columns).  A_i
-// is loaded once per pass and reused by all j; when 2 * s * NT <= 512 the
-// accumulators are double-buffered so the epilogue of pass i overlaps the MMAs
-// of pass i + 1.  The fp64/fp32 outer accumulator never leaves registers.
+// slice i, or per two A slices when their 2 * s accumulators fit TMEM: a full
+// K loop that accumulates the pair products A_i B_j for every j into s TMEM
+// accumulators of NT columns each (pa * s * NT <= 512 columns).  A_i is
+// loaded once per pass and reused by all j, and B's stack once per pass for
+// its pa A slices; when 2 * pa * s * NT <= 512 the accumulators are
+// double-buffered so the epilogue of one pass overlaps the MMAs of the next.
+// The fp64/fp32 outer accumulator never leaves registers.
 //
 // Every spin-wait is bounded (oz_common.cuh); on a timeout the kernel records
 // a code in g_device_status, drains its own asynchronous work (bounded), frees
