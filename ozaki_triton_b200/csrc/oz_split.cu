@@ -41,6 +41,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 #include <cudaTypedefs.h>
@@ -851,9 +852,12 @@ constexpr int kPairMaxStages = 6;
 constexpr int kPairSmem = 224 * 1024;
 constexpr int kPairHalf = kRowCTA / 2;          // threads per column
 
-// barrier over the 256 threads of one half of the CTA (ids 1 and 2)
+// barrier over the NT threads of one half of the CTA (ids 1 and 2)
+template <int NT = kPairHalf>
 __device__ __forceinline__ void half_sync(int half) {
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(kPairHalf) : "memory");
+  // immediate barrier ids, so that the kernel reserves three barriers, not all
+  if (half == 0) asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+  else asm volatile("bar.sync 2, %0;" ::"n"(NT) : "memory");
 }
 
 // FULL: the slice row is exactly the chunks' length (ld == NCH * 2048), so
@@ -952,6 +956,134 @@ __global__ void __launch_bounds__(kRowCTA, 1)
     };
     ll.run(s, alpha, reduce, emit, put_scale, [](int) {});
   }
+}
+
+// ---------------------------------------------------------------------------
+// fp64 column pairs with K split over a CTA pair (cluster of 2)
+// ---------------------------------------------------------------------------
+// For columns of 4097..8192 rows whose slice rows are 8192 elements long
+// (B of C3), with the fp32 residual.  A cluster of two CTAs takes a panel of
+// 2 columns; CTA r holds rows [r*4096, r*4096 + 4096) of it (64 KB, one
+// stage), so three CTAs fit per SM.  Each CTA half (128 threads) splits one
+// column: level 0 from shared memory (maximum, then quantisation into the
+// fp32 residual in registers), then the stage goes to the next panel's copy
+// and levels 1.. run from registers.  Per level each half reduces its part
+// of the column, writes its partial maximum into its own slot and sends it
+// to the peer CTA with an asynchronous remote store that completes on the
+// peer's exchange barrier; the exchange barriers and slots alternate by level
+// parity, so a value of level l + 1 can never complete level l's barrier.
+// Thread t of a half holds rows c*2048 + t + 128*e (c < 2, e < 16) of its
+// CTA's part: lane-consecutive rows for the shared-memory reads and stores.
+constexpr int kPairKRows = 4096;                // rows per CTA of the pair
+constexpr int kPairKThreads = 256;              // 128 per column
+constexpr int kPairKPerSM = 3;
+
+template <int SK>
+__global__ void __launch_bounds__(kPairKThreads, kPairKPerSM)
+    split_colpairs_kx(const __grid_constant__ CUtensorMap tm_in, int lines, int64_t panels,
+                      int ppb, int ld, int s, int alpha,
+                      typename SliceT<SK>::type *__restrict__ out, float *__restrict__ scales) {
+  using ST = typename SliceT<SK>::type;
+  using QT = typename QOut<SK>::type;
+  constexpr int T = kPairKThreads / 2, VEC = 16, NCH = kPairKRows / kPairRows, NV = NCH * VEC;
+  constexpr int STAGE = kPairKRows * 16;        // 64 KB: 2 columns x 4096 rows of fp64
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGE);
+  uint64_t *xbar = full + 1;                                   // [2 halves][2 parities]
+  float *slot = reinterpret_cast<float *>(xbar + 4);           // [2 halves][2 parities][2 ranks]
+  float *red = slot + 8;                                       // [2 halves][2 parities][4 warps]
+  const uint32_t rank = cluster_ctarank();
+  const int cid = blockIdx.x / 2, ncl = gridDim.x / 2;
+  const int half = threadIdx.x / T, tl = threadIdx.x % T;
+  const int kbase = (int)rank * kPairKRows;
+
+  auto issue = [&](int64_t panel) {
+    const int b = (int)(panel / ppb), n0 = (int)(panel % ppb) * 2;
+    mbar_arrive_expect_tx(full, (uint32_t)STAGE);
+#pragma unroll 1
+    for (int r = 0; r < kPairKRows; r += 256)
+      tma_load_3d(smem + r * 16, &tm_in, full, n0, kbase + r, b);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(full, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 1);
+    fence_mbar_init();
+    prefetch_tmap(&tm_in);
+  }
+  cluster_sync();                       // the peer's barriers exist before any remote store
+  if (threadIdx.x == 0 && cid < panels) issue(cid);
+
+  volatile int abort_flag = 0;
+  uint32_t lc = 0;                      // reductions of this half so far
+  auto reduce = [&](float m, int) -> float {
+    const int par = (int)(lc & 1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tl & 31) == 0) red[(half * 2 + par) * 4 + (tl >> 5)] = m;
+    half_sync<T>(half);
+    float *my = slot + (half * 2 + par) * 2;
+    uint64_t *xb = &xbar[half * 2 + par];
+    if (tl == 0) {
+      const float *r4 = red + (half * 2 + par) * 4;
+      const float v = fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]));
+      my[rank] = v;
+      mbar_arrive_expect_tx(xb, 4u);    // the peer's value; the own one is local
+      st_async_f32(map_to_cta(smem_u32(my + rank), rank ^ 1u), v,
+                   map_to_cta(smem_u32(xb), rank ^ 1u));
+    }
+    mbar_wait_bounded(xb, (lc >> 1) & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_CLUSTER);
+    ++lc;
+    return fmaxf(my[0], my[1]);
+  };
+
+  int it = 0;
+  for (int64_t pw = cid; pw < panels; pw += ncl, ++it) {
+    mbar_wait_bounded(full, it & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_PRODUCER);
+    const int b = (int)(pw / ppb), n0 = (int)(pw % ppb) * 2;
+    const int line = n0 + half;
+    const bool col_ok = line < lines;   // odd N: both CTAs still run the exchange
+    ST *row0 = out + ((int64_t)b * s * lines + (col_ok ? line : 0)) * (int64_t)ld + kbase + tl;
+    ST *dl = row0;
+    auto put_scale = [&](int l, float sc) {
+      if (rank == 0 && tl == 0 && col_ok) scales[((int64_t)b * s + l) * lines + line] = sc;
+      dl = row0 + (int64_t)l * lines * ld;
+    };
+    auto emit = [&](int, int i, QT qv) {
+      if (col_ok) dl[(i / VEC) * kPairRows + (i % VEC) * T] = to_slice<SK>(qv);
+    };
+    const double *src = reinterpret_cast<const double *>(smem) + half;
+    LineLevels<double, SK, NV, false, false> ll;
+    // level 0 from shared memory: the maximum, then the quantisation
+    double md = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      md = fmax(md, fabs(src[2 * ((i / VEC) * kPairRows + tl + (i % VEC) * T)]));
+    const float m = reduce(__double2float_rn(md), 0);
+    LevelP lv;
+    lv.init(m, alpha);
+    put_scale(0, lv.scale);
+    const bool upd = s > 1;
+    const double inv_d = lv.inv_d();
+    const double nscale = -(double)lv.scale;
+    auto level0 = [&](auto clamp_tag) {
+      constexpr bool C = decltype(clamp_tag)::value;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        double nd = 0.0;
+        float nf = 0.f;
+        const QT q = step_f64<SK, false, C>(src[2 * ((i / VEC) * kPairRows + tl + (i % VEC) * T)],
+                                            inv_d, nscale, upd, nd, nf);
+        ll.vf(i) = nf;
+        emit(0, i, q);
+      }
+    };
+    if (SK == OZ_I8 && m >= 127.25f * lv.scale) level0(std::true_type{});
+    else level0(std::false_type{});
+    __syncthreads();                     // the stage is read by both halves
+    if (threadIdx.x == 0 && pw + ncl < panels) issue(pw + ncl);
+    ll.run(s, alpha, reduce, emit, put_scale, [](int) {}, 1);
+  }
+  cluster_sync();                       // no CTA leaves while the peer may still address it
 }
 
 // ---------------------------------------------------------------------------
@@ -1516,6 +1648,90 @@ int launch_colpairs(const double *in, int64_t sb, int64_t sk, int64_t batch, int
   return full ? go(split_colpairs_tma<SK, 4, EXACT, true>) : go(split_colpairs_tma<SK, 4, EXACT, false>);
 }
 
+// fp64 columns of 4097..8192 rows with 8192-element slice rows and the fp32
+// residual: split_colpairs_kx (K split over a CTA pair, three CTAs per SM)
+// when its clusters can be resident three CTAs per SM; OZ_SPLIT_COLS=pairs
+// (read on every call) selects split_colpairs_tma.  Sets *done when it
+// launched.
+template <int SK>
+int launch_colpairs_kx(const double *in, int64_t sb, int64_t sk, int64_t batch, int lines, int K,
+                       int ld, int s, int alpha, void *slices, float *scales, cudaStream_t st,
+                       bool *done) {
+  using ST = typename SliceT<SK>::type;
+  *done = false;
+  const char *env = getenv("OZ_SPLIT_COLS");
+  if (env && strcmp(env, "pairs") == 0) return OZ_OK;
+  if (((uintptr_t)in % 16) != 0 || (sk * 8) % 16 != 0 || (sb * 8) % 16 != 0 ||
+      K <= kPairKRows || K > 2 * kPairKRows || ld != 2 * kPairKRows || lines < 1)
+    return OZ_OK;
+  const int smem = kPairKRows * 16 + 8 * 5 + 4 * 8 + 4 * 16;
+  static int resident = -1;
+  auto kern = split_colpairs_kx<SK>;
+  if (resident < 0) {
+    int nb = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kPairKThreads, smem) !=
+            cudaSuccess) {
+      (void)cudaGetLastError();
+      nb = 0;
+    }
+    resident = nb;
+  }
+  if (resident < kPairKPerSM) return OZ_OK;
+  auto enc = split_encode_fn();
+  if (!enc) return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)lines, (cuuint64_t)K, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(sk * 8), (cuuint64_t)(sb * 8)};
+  cuuint32_t box[3] = {2, 256, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 3, const_cast<double *>(in), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(OZ_ERR_CUDA, "cuTensorMapEncodeTiled (column pairs, K split) failed (%d)",
+                     (int)r);
+  const int ppb = (lines + 1) / 2;
+  const int64_t panels = (int64_t)ppb * batch;
+  const int clusters =
+      (int)std::min<int64_t>(panels, (int64_t)sm_count_split() * kPairKPerSM / 2);
+  if (int rc = set_smem_once((const void *)kern, smem, "cudaFuncSetAttribute(split_colpairs_kx)"))
+    return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(clusters * 2));
+  cfg.blockDim = dim3(kPairKThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launch();
+  *done = true;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, map, lines, panels, ppb, ld, s, alpha,
+                                       reinterpret_cast<ST *>(slices), scales),
+                    "split_colpairs_kx launch");
+}
+
+// fp64 columns: the K-split pair kernel where it applies, else the column-pair
+// kernel.  Sets *done when one of them launched.
+template <int SK, bool EXACT>
+int launch_fp64_cols(const double *in, int64_t sb, int64_t sk, int64_t batch, int lines, int K,
+                     int ld, int s, int alpha, void *slices, float *scales, cudaStream_t st,
+                     bool *done) {
+  if constexpr (!EXACT) {
+    int rc = launch_colpairs_kx<SK>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales, st,
+                                    done);
+    if (rc != OZ_OK || *done) return rc;
+  }
+  return launch_colpairs<SK, EXACT>(in, sb, sk, batch, lines, K, ld, s, alpha, slices, scales,
+                                    st, done);
+}
+
 template <typename TIn, int SK, bool EXACT>
 int launch_cols(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lines, int K, int ld,
                 int s, int alpha, void *slices, float *scales, cudaStream_t st, bool *done) {
@@ -1527,8 +1743,8 @@ int launch_cols(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int lines,
       K <= 0)
     return OZ_OK;
   if constexpr (sizeof(TIn) == 8) {
-    int rc = launch_colpairs<SK, EXACT>(in, sb, sk, batch, lines, K, ld, s, alpha, slices,
-                                        scales, st, done);
+    int rc = launch_fp64_cols<SK, EXACT>(in, sb, sk, batch, lines, K, ld, s, alpha, slices,
+                                         scales, st, done);
     if (rc != OZ_OK || *done) return rc;
   }
   // values per thread: the smallest V whose cluster of <= 8 CTAs covers ld
@@ -1719,10 +1935,11 @@ int split_impl(const void *in, int in_dtype, int64_t batch, int64_t lines, int64
     const double *ind = reinterpret_cast<const double *>(in);
     int rc;
 #define OZ_P(SK)                                                                             \
-  rc = exact ? launch_colpairs<SK, true>(ind, stride_b, stride_k, batch, (int)lines, (int)k,    \
-                                         (int)ld, num_splits, alpha, slices, scales, st, &done) \
-             : launch_colpairs<SK, false>(ind, stride_b, stride_k, batch, (int)lines, (int)k,   \
-                                          (int)ld, num_splits, alpha, slices, scales, st, &done); \
+  rc = exact ? launch_fp64_cols<SK, true>(ind, stride_b, stride_k, batch, (int)lines, (int)k,   \
+                                          (int)ld, num_splits, alpha, slices, scales, st, &done) \
+             : launch_fp64_cols<SK, false>(ind, stride_b, stride_k, batch, (int)lines, (int)k,  \
+                                           (int)ld, num_splits, alpha, slices, scales, st,       \
+                                           &done);                                               \
   break;
     switch (slice_dtype) {
       case OZ_I8: OZ_P(OZ_I8)

@@ -372,6 +372,34 @@ def test_split_fp64_column_pairs(sk, K, lines, s, residual):
     check_split(view, lines_np, s, alpha, sk, "fp64", residual=residual)
 
 
+@pytest.mark.parametrize("kind", ["default", "pairs"])
+@pytest.mark.parametrize("sk,K,lines,s", [("int8", 8192, 67, 4), ("int8", 8100, 64, 3),
+                                          ("fp16", 8192, 5, 2), ("int8", 8192, 1, 1)])
+def test_split_fp64_columns_k_split_over_a_cta_pair(kind, sk, K, lines, s, monkeypatch):
+    """fp64 columns of 4097..8192 rows with 8192-element slice rows go by
+    default to split_colpairs_kx (two CTAs of a cluster hold the upper and
+    lower half of a column pair and exchange each level's partial maxima);
+    OZ_SPLIT_COLS=pairs (read on every call) selects split_colpairs_tma.
+    Odd column counts, K short of 8192 (zero rows at the end), batch 2: one
+    launch, bit-exact against the oracle."""
+    if kind == "pairs":
+        monkeypatch.setenv("OZ_SPLIT_COLS", "pairs")
+    else:
+        monkeypatch.delenv("OZ_SPLIT_COLS", raising=False)
+    rng = np.random.default_rng(K + lines + s)
+    N = 80                                            # row pitch: 640 bytes
+    b = rand_lines(rng, (2, N, K), "fp64")
+    bd = to_dev(np.ascontiguousarray(np.swapaxes(b, -1, -2)), "fp64")   # (2, K, N)
+    view = bd[:, :, :lines].transpose(-1, -2)         # (2, lines, K), lines contiguous
+    lines_np = np.swapaxes(host(bd), -1, -2)[:, :lines]
+    alpha = oz.compute_split_bits(K, TDT[sk], oz.select_dot_accum_dtype(TDT[sk]))
+    from ozaki_triton_b200 import _lib
+    n0 = _lib.load().oz_launch_count()
+    check_split(view, lines_np, s, alpha, sk, "fp64")
+    assert _lib.load().oz_launch_count() - n0 == 1
+    assert oz.device_status() == 0
+
+
 def test_bounded_wait_times_out_and_the_context_stays_usable():
     """Failure detection without a GPU fault: a kernel waits on a barrier that
     nothing arrives on, gives up after a short bound (~0.1 s of SM cycles),
