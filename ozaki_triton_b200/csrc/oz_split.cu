@@ -1118,7 +1118,7 @@ __global__ void __launch_bounds__(kColCTA, 1)
   float *red = reinterpret_cast<float *>(outst + W * PITCH);        // [G][W]
   float *peer = red + G * W;                                        // [2][kMaxCluster][W]
   uint64_t *full = reinterpret_cast<uint64_t *>(peer + 2 * kMaxCluster * W);
-  uint64_t *xbar = full + 4;            // per-level exchange of column maxima
+  uint64_t *xbar = full + 4;            // [2] per-level exchange of column maxima, by parity
 
   const int CL = (int)cluster_nctarank();
   const int rank = (int)cluster_ctarank();
@@ -1136,7 +1136,8 @@ __global__ void __launch_bounds__(kColCTA, 1)
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
-    mbar_init(xbar, 1);
+    mbar_init(&xbar[0], 1);
+    mbar_init(&xbar[1], 1);
     fence_mbar_init();
     prefetch_tmap(&tm_in);
   }
@@ -1170,8 +1171,9 @@ __global__ void __launch_bounds__(kColCTA, 1)
     // Column maxima: CTA-local reduction, then every CTA sends its W partial
     // maxima to every CTA of the cluster with asynchronous remote stores that
     // complete on the receiver's exchange barrier (no cluster-wide barrier
-    // per level).  Slots are double-buffered by level parity: a CTA can only
-    // be one level ahead of a peer that still reads the other buffer.
+    // per level).  Slots and barriers alternate by level parity: a CTA can
+    // only be one level ahead of a peer that still reads the other buffer,
+    // and a value of level l + 1 cannot complete level l's barrier.
     auto reduce = [&](float m, int l) -> float {
       (void)l;
       const int pb = (int)(lc & 1);
@@ -1182,15 +1184,17 @@ __global__ void __launch_bounds__(kColCTA, 1)
         for (int gg = 1; gg < G; ++gg) mm = fmaxf(mm, red[gg * W + threadIdx.x]);
         float *slot = peer + (pb * kMaxCluster + rank) * W + threadIdx.x;
         if (CL > 1) {
-          if (threadIdx.x == 0) mbar_arrive_expect_tx(xbar, (uint32_t)(CL * W * 4));
-          const uint32_t a = smem_u32(slot), xb = smem_u32(xbar);
+          if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar[pb], (uint32_t)(CL * W * 4));
+          const uint32_t a = smem_u32(slot), xb = smem_u32(&xbar[pb]);
           for (int r = 0; r < CL; ++r)
             st_async_f32(map_to_cta(a, r), mm, map_to_cta(xb, r));
         } else {
           *slot = mm;
         }
       }
-      if (CL > 1) mbar_wait_bounded(xbar, lc & 1, (volatile int *)&abort_flag, DEV_TIMEOUT_CLUSTER);
+      if (CL > 1)
+        mbar_wait_bounded(&xbar[pb], (lc >> 1) & 1, (volatile int *)&abort_flag,
+                          DEV_TIMEOUT_CLUSTER);
       else __syncthreads();
       ++lc;
       float mm = peer[(pb * kMaxCluster) * W + c];
@@ -1554,7 +1558,7 @@ int launch_cols_v(const TIn *in, int64_t sb, int64_t sk, int64_t batch, int line
   constexpr int PITCH = KC * (int)sizeof(ST) + 16;
   const int CL = (ld + KC - 1) / KC;
   if (*done || CL > kMaxCluster) return OZ_OK;
-  const int fixed = W * PITCH + (G * W + 2 * kMaxCluster * W) * 4 + 8 * 5;
+  const int fixed = W * PITCH + (G * W + 2 * kMaxCluster * W) * 4 + 8 * 6;
   const int NS = min(4, (kColSmem - fixed) / STAGE);
   if (NS < 1) return OZ_OK;
   *done = true;
