@@ -222,6 +222,33 @@ int oz_cross_gemm_blocked(const void *a_slices, const void *b_slices, const floa
                           uint32_t flags, void *stream);
 
 /*
+ * oz_cross_gemm_blocked (one batch) in a single persistent launch while B's
+ * column blocks are still arriving (no counterpart in the reference, which
+ * has no multi-GPU path; it lets a rank multiply the blocks it pulls from its
+ * peers without one launch per block).
+ *
+ *   ready       : device int32[blocks]; block c is read (its slices and
+ *                 scales) once ready[c] == ready_value.  Write the flag with
+ *                 a copy ordered after the block's own copies on the same
+ *                 stream (e.g. a 4-byte copy from pinned host memory): the
+ *                 kernel holds every SM while it waits, so the flag must
+ *                 come from work that needs none, like a copy engine.
+ *   first_block, block_count : the launch computes the output columns of
+ *                 block_count blocks (0: all), first_block, first_block + 1,
+ *                 .. (mod blocks), in that order; other columns of C are
+ *                 left as they are.
+ * The waits are bounded (about 2 s of SM clock): a block that never arrives
+ * ends the launch early and oz_device_status then reports OZ_ERR_TIMEOUT
+ * (code 5).  All other arguments and the results as oz_cross_gemm_blocked.
+ */
+int oz_cross_gemm_arrivals(const void *a_slices, const void *b_slices, const float *a_scales,
+                           const float *b_scales, int64_t m, int64_t n, int64_t k, int64_t ld,
+                           int32_t num_splits, int slice_dtype, int out_dtype,
+                           int64_t b_block_cols, const int32_t *ready, int32_t ready_value,
+                           int32_t first_block, int32_t block_count, void *c, int64_t ldc,
+                           uint32_t flags, void *stream);
+
+/*
  * Peer mappings for the multi-GPU gather (no counterpart in the reference,
  * which has no multi-GPU path).  One process per GPU: a rank exports the
  * allocation holding its slice buffer, each peer imports it once and pulls
@@ -239,7 +266,8 @@ int oz_ipc_import(const void *handle, int64_t offset, void **ptr);
 /* Unmap what oz_ipc_import returned (same ptr and offset). */
 int oz_ipc_close(void *ptr, int64_t offset);
 
-/* Stream-ordered device-to-device copy; either side may be a peer mapping. */
+/* Stream-ordered copy (kind inferred from the addresses): device memory,
+ * a peer mapping or pinned host memory on either side. */
 int oz_copy_async(void *dst, const void *src, int64_t bytes, void *stream);
 
 /*

@@ -41,6 +41,8 @@ SIGNATURES = {
                              _vp, _vp, _i64, _i64, _vp, _i64, _u32, _vp]),
     "oz_cross_gemm_blocked": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _int,
                                      _int, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _u32, _vp]),
+    "oz_cross_gemm_arrivals": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _int,
+                                      _int, _i64, _vp, _i32, _i32, _i32, _vp, _i64, _u32, _vp]),
     "oz_matmul_workspace_bytes": (_i64, [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                          _i64, _i32, _int]),
     "oz_matmul": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64,

@@ -92,6 +92,7 @@ enum DeviceCode : int {
   DEV_TIMEOUT_MMA = 2,
   DEV_TIMEOUT_EPILOGUE = 3,
   DEV_TIMEOUT_CLUSTER = 4,
+  DEV_TIMEOUT_ARRIVAL = 5,    // oz_cross_gemm_arrivals: a column block never arrived
   DEV_TIMEOUT_SELFTEST = 9,   // oz_wait_selftest: a wait that nothing satisfies
 };
 

@@ -63,6 +63,13 @@ struct GemmParams {
   int stages;            // pipeline depth
   int pa;                // A slices per pass (1, or 2 when 2 * s * NT fits the 512 TMEM columns)
   uint32_t idesc;        // instruction descriptor without the N field
+  // column blocks still arriving (oz_cross_gemm_arrivals; ready == nullptr:
+  // every block present): the tiles of block_count blocks go block by block
+  // from first_block on, and block c is read once ready[c] == ready_value
+  const int *ready;
+  int ready_value;
+  int first_block;
+  int tiles_bn;          // column tiles per column block
 };
 
 // One pipeline stage holds, for one 128-byte K block, the A tiles of the
@@ -107,19 +114,64 @@ to_out(typename OutT<OUTK>::acc v) {
 
 // tile t -> (batch b, row tile mb, column tile nb) in a grouped raster:
 // GM row tiles sweep all column tiles before moving on, so the A rows and B
-// columns of the tiles running at the same time stay in L2.
-__device__ __forceinline__ void tile_coords(const GemmParams &p, int t, int &b, int &mb, int &nb) {
-  const int tpb = p.tiles_m * p.tiles_n;
-  b = t / tpb;
-  int local = t - b * tpb;
+// columns of the tiles running at the same time stay in L2.  With arriving
+// column blocks the tiles go block by block in arrival order (first_block,
+// first_block + 1, .. modulo the number of blocks, one batch), the same
+// raster inside each block; blk is the tile's column block.  Returns false
+// for a tile past the last column (a short last block), which every role
+// skips.
+__device__ __forceinline__ bool tile_coords(const GemmParams &p, int t, int &b, int &mb, int &nb,
+                                            int &blk) {
   const int GM = p.gm;
-  int per_group = GM * p.tiles_n;
+  int local, cols, nb0 = 0;
+  if (p.ready) {
+    const int tpb = p.tiles_m * p.tiles_bn;
+    const int ord = t / tpb;
+    b = 0;
+    local = t - ord * tpb;
+    blk = (p.first_block + ord) % p.bblocks;
+    cols = p.tiles_bn;
+    nb0 = blk * p.tiles_bn;
+  } else {
+    const int tpb = p.tiles_m * p.tiles_n;
+    b = t / tpb;
+    local = t - b * tpb;
+    cols = p.tiles_n;
+  }
+  int per_group = GM * cols;
   int group = local / per_group;
   int first_m = group * GM;
   int gsz = min(p.tiles_m - first_m, GM);
   int in_group = local - group * per_group;
   mb = first_m + in_group % gsz;
-  nb = in_group / gsz;
+  nb = nb0 + in_group / gsz;
+  if (!p.ready) blk = 0;
+  return nb < p.tiles_n;
+}
+
+// Bounded wait for a column block's arrival flag (acquire, then ordered
+// before the async proxy's TMA reads of the block).  The flag is written by
+// a copy engine, which needs no SM, so waiting here cannot starve the writer.
+__device__ __forceinline__ bool wait_block(const GemmParams &p, int blk, uint64_t &seen,
+                                           volatile int *abort_flag) {
+  if (!p.ready || (blk < 64 && ((seen >> blk) & 1))) return true;
+  const int *f = p.ready + blk;
+  const long long t0 = clock64();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v == p.ready_value) break;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBoundCycles) {
+      *abort_flag = DEV_TIMEOUT_ARRIVAL;
+      atomicCAS(&g_device_status, 0, (int)DEV_TIMEOUT_ARRIVAL);
+      return false;
+    }
+    __nanosleep(200);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  if (blk < 64) seen |= 1ull << blk;
+  return true;
 }
 
 // PAIR == 1: one CTA computes a 128 x NT tile with cta_group::1 MMAs.
@@ -220,9 +272,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t it = 0;           // running stage counter (slot = it % S)
       bool ok = true;
       const uint32_t tx = (uint32_t)(PAIR * sbytes);
+      uint64_t seen = 0;         // column blocks known to have arrived
       for (int t = unit; ok && t < p.num_tiles; t += units) {
-        int b, mb, nb;
-        tile_coords(p, t, b, mb, nb);
+        int b, mb, nb, ablk;
+        if (!tile_coords(p, t, b, mb, nb, ablk)) continue;
+        if (!(ok = wait_block(p, ablk, seen, abort_flag))) break;
         const int ai = p.a_index ? p.a_index[b] : b;
         const int bi = p.b_index ? p.b_index[b] : b;
         const int arow = mb * TM + (int)rank * kBM;
@@ -271,6 +325,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       };
       for (int t = unit; ok && t < p.num_tiles; t += units) {
+        int b_, mb_, nb_, blk_;
+        if (!tile_coords(p, t, b_, mb_, nb_, blk_)) continue;
         for (int i = 0; ok && i < s; i += PA, ++pass) {
           const int buf = pass % nbuf;
           const uint32_t use = pass / nbuf;
@@ -336,11 +392,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
     for (int x = 0; x < NH; ++x) out[x] = (ACC)0;
     uint32_t pass = 0;
-    int tile_iter = 0;
+    int tile_iter = -1;                       // tiles of this CTA processed, minus one
     bool ok = true;
-    for (int t = unit; ok && t < p.num_tiles; t += units, ++tile_iter) {
-      int b, mb, nb;
-      tile_coords(p, t, b, mb, nb);
+    uint64_t seen = 0;                        // column blocks known to have arrived
+    for (int t = unit; ok && t < p.num_tiles; t += units) {
+      int b, mb, nb, ablk;
+      if (!tile_coords(p, t, b, mb, nb, ablk)) continue;
+      ++tile_iter;
+      // the B scales of an arriving block are read only once it is here
+      ok = __all_sync(0xffffffffu, wait_block(p, ablk, seen, abort_flag));
+      if (!ok) break;
       const int ai = p.a_index ? p.a_index[b] : b;
       const int bi = p.b_index ? p.b_index[b] : b;
       const int m = mb * TM + row;
@@ -606,7 +667,9 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
                     int64_t ld, int32_t num_splits, int slice_dtype, int out_dtype,
                     const int32_t *a_index, const int32_t *b_index, int64_t a_batches,
                     int64_t b_batches, int64_t b_block_cols, void *c, int64_t ldc,
-                    uint32_t flags, void *stream) {
+                    uint32_t flags, void *stream, const int32_t *ready = nullptr,
+                    int32_t ready_value = 0, int32_t first_block = 0,
+                    int32_t block_count = 0) {
   if (num_splits < 1 || num_splits > 8)
     return set_error(OZ_ERR_INVALID, "num_splits must be in [1, 8], got %d", num_splits);
   if (batch < 0 || m < 0 || n < 0 || k < 0)
@@ -648,6 +711,14 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
     return set_error(OZ_ERR_INVALID, "bad operand batch counts");
   const int64_t bw = b_block_cols == 0 ? n : b_block_cols;
   const int64_t bblocks = (n + bw - 1) / bw;
+  if (ready && (batch != 1 || b_block_cols <= 0 || first_block < 0 || first_block >= bblocks ||
+                block_count < 0 || block_count > bblocks))
+    return set_error(OZ_ERR_INVALID,
+                     "arriving column blocks need batch 1, a block width, a first block in "
+                     "[0, %lld) and at most that many blocks (batch=%lld, width=%lld, first=%d, "
+                     "count=%d)",
+                     (long long)bblocks, (long long)batch, (long long)b_block_cols, first_block,
+                     block_count);
   if (m > INT32_MAX || n > INT32_MAX || bw > INT32_MAX || a_batches * num_splits > INT32_MAX ||
       b_batches * bblocks * num_splits > INT32_MAX)
     return set_error(OZ_ERR_INVALID, "size out of range");
@@ -705,6 +776,15 @@ int cross_gemm_impl(const void *a_slices, const void *b_slices, const float *a_s
   p.stages = min(kMaxStages, (kSmemBudget - scale_stage_bytes(num_splits, nt)) /
                                  stage_bytes(num_splits, nt, pair, pa));
   if (tc.stages > 0 && tc.stages < p.stages) p.stages = tc.stages;
+  p.ready = ready;
+  p.ready_value = ready_value;
+  p.first_block = first_block;
+  p.tiles_bn = (int)(bw / nt);        // bw is a multiple of 128, nt of 64
+  if (ready) {
+    tiles = (block_count ? block_count : bblocks) * p.tiles_m * p.tiles_bn;
+    if (tiles > INT32_MAX) return set_error(OZ_ERR_INVALID, "too many tiles");
+    p.num_tiles = (int)tiles;
+  }
 
   cudaEvent_t ev0 = g_prof_begin, ev1 = g_prof_end;
   g_prof_begin = g_prof_end = nullptr;
@@ -778,4 +858,17 @@ extern "C" int oz_cross_gemm_blocked(const void *a_slices, const void *b_slices,
   return oz::cross_gemm_impl(a_slices, b_slices, a_scales, b_scales, batch, m, n, k, ld,
                              num_splits, slice_dtype, out_dtype, a_index, b_index, a_batches,
                              b_batches, b_block_cols, c, ldc, flags, stream);
+}
+
+extern "C" int oz_cross_gemm_arrivals(const void *a_slices, const void *b_slices,
+                                      const float *a_scales, const float *b_scales, int64_t m,
+                                      int64_t n, int64_t k, int64_t ld, int32_t num_splits,
+                                      int slice_dtype, int out_dtype, int64_t b_block_cols,
+                                      const int32_t *ready, int32_t ready_value,
+                                      int32_t first_block, int32_t block_count, void *c,
+                                      int64_t ldc, uint32_t flags, void *stream) {
+  if (!ready) return oz::set_error(OZ_ERR_INVALID, "null arrival flags");
+  return oz::cross_gemm_impl(a_slices, b_slices, a_scales, b_scales, 1, m, n, k, ld, num_splits,
+                             slice_dtype, out_dtype, nullptr, nullptr, 1, 1, b_block_cols, c, ldc,
+                             flags, stream, ready, ready_value, first_block, block_count);
 }

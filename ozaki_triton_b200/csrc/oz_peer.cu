@@ -79,7 +79,7 @@ extern "C" int oz_copy_async(void *dst, const void *src, int64_t bytes, void *st
   using namespace oz;
   if (bytes < 0 || (bytes > 0 && (!dst || !src))) return set_error(OZ_ERR_INVALID, "bad argument");
   if (bytes == 0) return OZ_OK;
-  return check_cuda(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice,
+  return check_cuda(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault,
                                     reinterpret_cast<cudaStream_t>(stream)),
                     "cudaMemcpyAsync");
 }

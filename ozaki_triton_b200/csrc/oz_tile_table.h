@@ -48,6 +48,9 @@ constexpr TileEntry kTileTable[] = {
     // 0.926 ms), but on 8 GPUs, with blocks arriving one by one, that setting
     // gave 1043 TFLOPS against 1107 for this entry with 2 GEMM streams
     {0, 4, 1, 1024, 1024, 8192, 1, 64, 16, 0},
+    // one rank's 1024 rows x all 8192 columns (eight 1024-column blocks) in one
+    // launch, every block present:      0.778 / 0.811 (2,64); 0.851 (2,128)
+    {0, 4, 1, 1024, 8192, 8192, 1, 64, 16, 0},
     {0, 4, 1, 2048, 16384, 16384, 2, 128, 16, 0},      // 6.73 / 8.32 (1,128)
 };
 

@@ -533,6 +533,135 @@ def test_gemm_column_blocked_b_bit_identical(n, w, sk, tile, monkeypatch):
     assert oz.device_status() == 0
 
 
+def _blocked_operands(n, w, sk, seed=5, M=300, K=520, s=3):
+    """A's slices, B's slices in the plain and in the column-blocked layout
+    (unused rows of the last block hold garbage), and the plain GEMM's C."""
+    from ozaki_triton_b200 import api
+    from ozaki_triton_b200 import dist as ozd
+    rng = np.random.default_rng(seed)
+    a = to_dev(rng.standard_normal((1, M, K)), "fp64")
+    b = to_dev(rng.standard_normal((1, K, n)), "fp64")
+    sd = TDT[sk]
+    alpha = oz.compute_split_bits(K, sd, oz.select_dot_accum_dtype(sd))
+    a_sl, a_sc = api._split_lines(a, a.stride(1), a.stride(2), M, K, s, alpha, sd, 0)
+    b_sl, b_sc = api._split_lines(b, b.stride(2), b.stride(1), n, K, s, alpha, sd, 0)
+    want = ozd.Backend().gemm(a_sl, b_sl, a_sc, b_sc, 1, M, n, K, s, torch.float64, False)
+    blocks = -(-n // w)
+    ld = b_sl.shape[-1]
+    g_sl = torch.full((1, blocks, s, w, ld), 77, dtype=torch.int8, device=DEV).view(sd) \
+        if sk != "fp32" else torch.full((1, blocks, s, w, ld), 3.0e30, device=DEV)
+    if sk == "fp16":
+        g_sl = torch.full((1, blocks, s, w, ld), 6.0e4, dtype=sd, device=DEV)
+    g_sc = torch.full((1, blocks, s, w), 1.0e30, device=DEV)
+    for c in range(blocks):
+        c0, c1 = c * w, min(n, (c + 1) * w)
+        g_sl[0, c, :, :c1 - c0] = b_sl[0, :, c0:c1]
+        g_sc[0, c, :, :c1 - c0] = b_sc[0, :, c0:c1]
+    return dict(a_sl=a_sl, a_sc=a_sc, g_sl=g_sl, g_sc=g_sc, want=want, M=M, K=K, s=s,
+                blocks=blocks)
+
+
+@pytest.mark.parametrize("n,w,sk,tile,first,count", [(600, 256, "int8", "2,128", 1, 0),
+                                                     (1000, 128, "int8", "1,64", 7, 0),
+                                                     (700, 128, "fp16", "2,128", 0, 0),
+                                                     (1024, 256, "int8", "1,64", 3, 3),
+                                                     (1000, 128, "int8", "1,64", 5, 7),
+                                                     (130, 128, "fp32", "2,64", 1, 1)])
+def test_gemm_arriving_blocks_bit_identical(n, w, sk, tile, first, count, monkeypatch):
+    """oz_cross_gemm_arrivals (one launch over column blocks that are still
+    arriving, tiles in arrival order from first_block on) gives the bits of
+    oz_cross_gemm on the columns of its block_count blocks and leaves the
+    others alone: with every flag set before the launch, and with the flags
+    set by copies on another stream that are held back behind a large
+    host-to-device copy, so that the kernel waits for them.  A short last
+    block (n = 600 with 256-column blocks: a tile past n that is skipped),
+    garbage in the unused rows, every slice kind, all blocks or all but
+    one (the multi-GPU use: every block except the rank's own)."""
+    from ozaki_triton_b200 import dist as ozd
+    from ozaki_triton_b200 import _lib
+    monkeypatch.setenv("OZ_GEMM_TILE", tile)
+    o = _blocked_operands(n, w, sk)
+    be = ozd.Backend()
+    lib = _lib.load()
+    blocks = o["blocks"]
+    run = [(first + i) % blocks for i in range(count or blocks)]
+    cols = torch.zeros(n, dtype=torch.bool)
+    for c in run:
+        cols[c * w:(c + 1) * w] = True
+    want = torch.where(cols.to(DEV), o["want"], torch.full_like(o["want"], -7.0))
+    flags = torch.ones(blocks, dtype=torch.int32, device=DEV)
+    got = torch.full_like(o["want"], -7.0)
+    be.gemm(o["a_sl"], o["g_sl"], o["a_sc"], o["g_sc"], 1, o["M"], n, o["K"], o["s"],
+            torch.float64, False, out=got, b_block_cols=w, ready=flags, first_block=first,
+            block_count=count)
+    torch.cuda.synchronize()
+    assert oz.device_status() == 0
+    assert torch.equal(got, want)
+    # late flags: a copy stream sets them after ~200 MB of host-to-device copy
+    flags.zero_()
+    big_h = torch.empty(200 << 20, dtype=torch.uint8, pin_memory=True)
+    big_d = torch.empty(200 << 20, dtype=torch.uint8, device=DEV)
+    one_h = torch.ones(1, dtype=torch.int32, pin_memory=True)
+    side = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        big_d.copy_(big_h, non_blocking=True)
+        for c in range(o["blocks"]):
+            _lib.check(lib.oz_copy_async(flags.data_ptr() + 4 * c, one_h.data_ptr(), 4,
+                                         side.cuda_stream))
+    got2 = torch.full_like(o["want"], -7.0)
+    be.gemm(o["a_sl"], o["g_sl"], o["a_sc"], o["g_sc"], 1, o["M"], n, o["K"], o["s"],
+            torch.float64, False, out=got2, b_block_cols=w, ready=flags, first_block=first,
+            block_count=count)
+    torch.cuda.synchronize()
+    assert oz.device_status() == 0
+    assert torch.equal(got2, want)
+
+
+def test_gemm_arriving_block_that_never_arrives_times_out():
+    """Failure detection without a GPU fault: a column block whose flag is
+    never set makes the one-launch GEMM give up after its bounded wait (about
+    2 s of SM clock), record code 5 and return; the host reads the timeout,
+    and the next computation on the same context is correct."""
+    from ozaki_triton_b200 import dist as ozd
+    from ozaki_triton_b200 import _lib
+    o = _blocked_operands(512, 256, "int8")
+    be = ozd.Backend()
+    flags = torch.tensor([1, 0], dtype=torch.int32, device=DEV)   # block 1 never arrives
+    assert oz.device_status() == 0
+    be.gemm(o["a_sl"], o["g_sl"], o["a_sc"], o["g_sc"], 1, o["M"], 512, o["K"], o["s"],
+            torch.float64, False, b_block_cols=256, ready=flags, first_block=0)
+    torch.cuda.synchronize()
+    with pytest.raises(_lib.OzakiError) as ei:
+        oz.device_status()
+    assert ei.value.status == _lib.OZ_ERR_TIMEOUT and "code 5" in str(ei.value)
+    assert oz.device_status() == 0
+    flags[1] = 1
+    got = be.gemm(o["a_sl"], o["g_sl"], o["a_sc"], o["g_sc"], 1, o["M"], 512, o["K"], o["s"],
+                  torch.float64, False, b_block_cols=256, ready=flags, first_block=0)
+    torch.cuda.synchronize()
+    assert oz.device_status() == 0
+    assert torch.equal(got, o["want"])
+
+
+def test_gemm_arrivals_argument_errors():
+    from ozaki_triton_b200 import _lib
+    lib = _lib.load()
+    o = _blocked_operands(512, 256, "int8")
+    flags = torch.ones(2, dtype=torch.int32, device=DEV)
+    c = torch.empty((1, o["M"], 512), dtype=torch.float64, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    args = lambda ready, first, width, count=0: (o["a_sl"].data_ptr(), o["g_sl"].data_ptr(),
+                                        o["a_sc"].data_ptr(), o["g_sc"].data_ptr(), o["M"], 512,
+                                        o["K"], o["a_sl"].shape[-1], o["s"], _lib.OZ_I8,
+                                        _lib.OZ_F64, width, ready, 1, first, count,
+                                        c.data_ptr(), 512, 0, st)
+    assert lib.oz_cross_gemm_arrivals(*args(None, 0, 256)) == _lib.OZ_ERR_INVALID
+    assert lib.oz_cross_gemm_arrivals(*args(flags.data_ptr(), 2, 256)) == _lib.OZ_ERR_INVALID
+    assert lib.oz_cross_gemm_arrivals(*args(flags.data_ptr(), 0, 0)) == _lib.OZ_ERR_INVALID
+    assert lib.oz_cross_gemm_arrivals(*args(flags.data_ptr(), 0, 256, 3)) == _lib.OZ_ERR_INVALID
+
+
 @pytest.mark.parametrize("use_ws", [False, True])
 @pytest.mark.parametrize("ik,sk,K,N", [("fp64", "int8", 8192, 70), ("fp64", "int8", 300, 70),
                                        ("fp32", "fp16", 1000, 70), ("bf16", "int8", 2048, 70),
