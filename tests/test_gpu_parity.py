@@ -376,21 +376,22 @@ def test_split_fp64_column_pairs(sk, K, lines, s, residual):
 @pytest.mark.parametrize("sk,K,lines,s", [("int8", 8192, 67, 4), ("int8", 8100, 64, 3),
                                           ("fp16", 8192, 5, 2), ("int8", 8192, 1, 1),
                                           ("int8", 8065, 33, 4), ("bf16", 8130, 6, 3),
-                                          ("fp32", 8192, 3, 2), ("int8", 8192, 601, 8)])
+                                          ("fp32", 8192, 3, 2), ("int8", 8192, 601, 8),
+                                          ("int8", 8192, 66, 4), ("fp16", 8192, 7, 3)])
 def test_split_fp64_columns_k_split_over_a_cta_pair(kind, sk, K, lines, s, monkeypatch):
     """fp64 columns of 4097..8192 rows with 8192-element slice rows go by
     default to split_colpairs_kx (two CTAs of a cluster hold the upper and
     lower half of a column pair and exchange each level's partial maxima);
     OZ_SPLIT_COLS=pairs (read on every call) selects split_colpairs_tma.
-    Odd column counts (a last panel of one column), K short of 8192 (zero
-    rows at the end), every slice type, up to 8 levels, more panels than
-    clusters, batch 2: one launch, bit-exact against the oracle."""
+    Odd and even column counts, K short of 8192 (zero rows at the end), every
+    slice type, up to 8 levels, more panels than clusters, batch 2: one
+    launch, bit-exact against the oracle."""
     if kind == "pairs":
         monkeypatch.setenv("OZ_SPLIT_COLS", "pairs")
     else:
         monkeypatch.delenv("OZ_SPLIT_COLS", raising=False)
     rng = np.random.default_rng(K + lines + s)
-    N = max(80, lines + 15)                           # row pitch: a multiple of 16 bytes
+    N = max(80, (lines + 16) // 2 * 2)                # row pitch: a multiple of 16 bytes
     b = rand_lines(rng, (2, N, K), "fp64")
     bd = to_dev(np.ascontiguousarray(np.swapaxes(b, -1, -2)), "fp64")   # (2, K, N)
     view = bd[:, :, :lines].transpose(-1, -2)         # (2, lines, K), lines contiguous
