@@ -293,7 +293,15 @@ def main():
                     help="1 GPU: time CUDA-graph replays of the step (launch-bound small configs)")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, DGEMM or CPU legs): the ncu command line")
+    ap.add_argument("--emulate-rank", type=int, default=0, metavar="N",
+                    help="1 GPU, diagnostic: one rank's GEMM phase of the N-GPU C3 p2p layout "
+                         "with every column block present, per-block launches against the "
+                         "one-launch peer GEMM")
     args = ap.parse_args()
+    if args.emulate_rank:
+        import bench_dist
+        bench_dist.emulate_rank(args)
+        return
     if args.profile:
         args.no_e2e = args.no_cpu_baseline = args.no_dgemm = True
     if args.impl == "reference":

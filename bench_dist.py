@@ -391,5 +391,102 @@ def run_batches(args, rank, world, dev):
     }
 
 
+def emulate_rank(args):
+    """One rank's GEMM phase of the N-GPU C3 p2p layout, on one GPU, with every
+    column block already present (a diagnostic of the transport's GEMM
+    scheduling; the transfer itself is not emulated).  Rank 0's rows of A
+    (M / N of them) times all of B in N column blocks of the blocked layout
+    the transport fills, three ways: one oz_cross_gemm_blocked launch per
+    block (the own block on the current stream, the others alternating over
+    two side streams, P2P_ONE_LAUNCH = False), the own block's launch plus one
+    oz_cross_gemm_arrivals launch over the other blocks (the transport's
+    default), and one arrivals launch over all blocks.  CUDA events, median of
+    20 after 3 warm-up runs; every variant's C is compared bit for bit with
+    the first's."""
+    import bench
+    import ozaki_triton_b200 as oz
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    world = args.emulate_rank
+    M, N, K, S = bench.M, bench.N, bench.K, bench.NUM_SPLITS
+    m = M // world
+    w = ozd.block_width(N, world)
+    blocks = -(-N // w)
+    a_h, b_h = bench.make_inputs()
+    A = a_h[:m].to(dev)
+    B = b_h.to(dev)
+    sd = torch.int8
+    alpha = ozd.compute_split_bits(K, sd, ozd.select_dot_accum_dtype(sd))
+    be = ozd.Backend()
+    A3 = A.reshape(1, m, K)
+    a_sl, a_sc = be.split(A3, A3.stride(1), A3.stride(2), m, K, S, alpha, sd, 0)
+    ld = a_sl.shape[-1]
+    sl = torch.zeros((1, blocks, S, w, ld), dtype=sd, device=dev)
+    sc = torch.zeros((1, blocks, S, w), dtype=torch.float32, device=dev)
+    for j in range(blocks):
+        ozd._split_block(be, B[:, j * w:min(N, (j + 1) * w)], K, S, alpha, sd, 0, sl[0, j],
+                         sc[0, j])
+    ready = torch.ones(blocks, dtype=torch.int32, device=dev)
+    c = torch.empty((1, m, N), dtype=torch.float64, device=dev)
+    cur = torch.cuda.current_stream(dev)
+    side = [torch.cuda.Stream(dev) for _ in range(2)]
+
+    def own_block():
+        be.gemm(a_sl, sl[:, 0:1], a_sc, sc[:, 0:1], 1, m, min(N, w), K, S, torch.float64, False,
+                out=c, col0=0, b_block_cols=w, stream=cur)
+
+    def per_block():
+        own_block()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        for st in side:
+            st.wait_event(ev)
+        for j in range(1, blocks):
+            c0, c1 = j * w, min(N, (j + 1) * w)
+            be.gemm(a_sl, sl[:, j:j + 1], a_sc, sc[:, j:j + 1], 1, m, c1 - c0, K, S,
+                    torch.float64, False, out=c, col0=c0, b_block_cols=w,
+                    stream=side[(j - 1) % 2])
+        for st in side:
+            cur.wait_stream(st)
+
+    def own_plus_arrivals():
+        own_block()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        side[0].wait_event(ev)
+        be.gemm(a_sl, sl, a_sc, sc, 1, m, N, K, S, torch.float64, False, out=c, b_block_cols=w,
+                stream=side[0], ready=ready, first_block=1 % blocks, block_count=blocks - 1)
+        cur.wait_stream(side[0])
+
+    def one_launch():
+        be.gemm(a_sl, sl, a_sc, sc, 1, m, N, K, S, torch.float64, False, out=c, b_block_cols=w,
+                stream=cur, ready=ready, first_block=0)
+
+    out, ref = {}, None
+    for name, fn in (("per_block_launches", per_block),
+                     ("own_block_plus_one_peer_launch", own_plus_arrivals),
+                     ("one_launch_all_blocks", one_launch)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(20):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            fn()
+            e1.record(cur)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        if ref is None:
+            ref = c.clone()
+        out[name] = {"median_ms": statistics.median(ts), "min_ms": min(ts),
+                     "same_bits": bool(torch.equal(c, ref))}
+        c.fill_(float("nan"))
+    print(json.dumps({"emulated_rank_of": world, "rows": m, "block_cols": w, "blocks": blocks,
+                      "config": "C3 rank 0: FP64->INT8 s=4, K = 8192, every block present",
+                      "device_status": oz.device_status(), **out}))
+
+
 def local_index(dev):
     return dev.index if dev.index is not None else torch.cuda.current_device()

@@ -377,6 +377,8 @@ class PeerBlocks:
         # which the GEMM holding every SM cannot starve.
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
         self.zeros_h = torch.zeros(self.world, dtype=torch.int32, pin_memory=True)
+        self.own_h = torch.zeros(self.world, dtype=torch.int32, pin_memory=True)
+        self.own_h[self.rank] = 1                 # the reset of "all": the own block is here
         self.one_h = torch.ones(1, dtype=torch.int32, pin_memory=True)
         self.reset_done = torch.cuda.Event()
 
@@ -405,13 +407,20 @@ _PEER_CACHE: Dict[tuple, PeerBlocks] = {}
 # a 1-GPU emulation with every block already present favoured them).
 P2P_COPY_STREAMS = 1
 P2P_GEMM_STREAMS: Optional[int] = 2
-# The peer blocks' GEMMs in one persistent launch instead
-# (oz_cross_gemm_arrivals), each block's tiles as its arrival flag is set; the
-# own block's GEMM still starts at once on the current stream.  A 1-GPU
-# emulation of a rank's GEMM phase at 8 GPUs (C3, every block present):
-# 0.778 ms for one launch over all blocks against 0.891 ms for eight block
-# GEMMs on 2 streams.  Used when every rank owns a block.
-P2P_ONE_LAUNCH = True
+# One persistent GEMM launch (oz_cross_gemm_arrivals) that takes each block's
+# tiles as its arrival flag is set, used when every rank owns a block:
+#   "all"   : every block in the launch, the own block's tiles first; the
+#             launch waits for the barrier (its copies' only kernel dependency)
+#   "peers" : the own block's GEMM at once on the current stream, the peer
+#             blocks in the launch
+#   None    : one GEMM launch per peer block, on two side streams.
+# `python bench.py --emulate-rank N` times a rank's GEMM phase the three ways
+# on one GPU with every block present (C3: 0.746 / 0.853 / 0.872 ms at 8,
+# 1.443 / 1.637 / 1.628 ms at 4 GPUs), but the transfer and the barrier turn
+# that order around on the GPUs themselves: C3 on 4 B200s 685.5 / 688.0
+# TFLOPS with "all" against 692.6 / 693.0 with "peers" (alternating runs), on
+# 8 B200s 1196-1200 with "peers" against 1162 per block.
+P2P_ONE_LAUNCH: Optional[str] = "peers"
 
 
 def p2p_status(group=None) -> str:
@@ -481,7 +490,8 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
     blocks = -(-n // w)
     order = [j for j in ((rank + d) % world for d in range(1, world)) if j < blocks]
     lib = _lib.load()
-    if P2P_ONE_LAUNCH and blocks == world and world > 1:
+    if P2P_ONE_LAUNCH in ("all", "peers") and blocks == world and world > 1:
+        every = P2P_ONE_LAUNCH == "all"
         # copies in ring order behind a reset of the arrival flags, each
         # block followed by its flag.  The own block's GEMM runs at once on
         # the current stream; the peer blocks' launch waits for the reset (so
@@ -491,7 +501,8 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
         cs, gs = copy_streams[0], gemm_streams[0]
         fl = pb.flags.data_ptr()
         cs.wait_event(pb.ready)
-        _lib.check(lib.oz_copy_async(fl, pb.zeros_h.data_ptr(), 4 * world, cs.cuda_stream))
+        _lib.check(lib.oz_copy_async(fl, (pb.own_h if every else pb.zeros_h).data_ptr(),
+                                     4 * world, cs.cuda_stream))
         pb.reset_done.record(cs)
         for j in order:
             d_sl, s_sl, n_sl, d_sc, s_sc, n_sc = copies[j]
@@ -499,15 +510,17 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
             _lib.check(lib.oz_copy_async(d_sc, s_sc, n_sc, cs.cuda_stream))
             _lib.check(lib.oz_copy_async(fl + 4 * j, pb.one_h.data_ptr(), 4, cs.cuda_stream))
         c = torch.empty((1, m_loc, n), dtype=A_local.dtype, device=dev)
-        b_sl, b_sc = views[rank]
-        backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, min(n, (rank + 1) * w) - rank * w, k,
-                     num_splits, A_local.dtype, skip_tail, out=c, col0=rank * w,
-                     b_block_cols=w, stream=cur)
+        if not every:
+            b_sl, b_sc = views[rank]
+            backend.gemm(a_sl, b_sl, a_sc, b_sc, 1, m_loc, min(n, (rank + 1) * w) - rank * w,
+                         k, num_splits, A_local.dtype, skip_tail, out=c, col0=rank * w,
+                         b_block_cols=w, stream=cur)
         gs.wait_event(pb.a_ready)
         gs.wait_event(pb.reset_done)
         backend.gemm(a_sl, sl, a_sc, sc, 1, m_loc, n, k, num_splits, A_local.dtype, skip_tail,
                      out=c, b_block_cols=w, stream=gs, ready=pb.flags,
-                     first_block=(rank + 1) % world, block_count=world - 1)
+                     first_block=rank if every else (rank + 1) % world,
+                     block_count=0 if every else world - 1)
         cur.wait_stream(gs)
         cur.wait_stream(cs)
         return c
