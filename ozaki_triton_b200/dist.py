@@ -493,10 +493,11 @@ def _sharded_p2p(backend, A_local, B_local, num_splits, slice_dtype, alpha, mode
     if P2P_ONE_LAUNCH in ("all", "peers") and blocks == world and world > 1:
         every = P2P_ONE_LAUNCH == "all"
         # copies in ring order behind a reset of the arrival flags, each
-        # block followed by its flag.  The own block's GEMM runs at once on
-        # the current stream; the peer blocks' launch waits for the reset (so
-        # no flag of the previous call is seen), which follows the barrier:
-        # the NCCL kernel has finished before a kernel holding every SM waits
+        # block followed by its flag.  "peers": the own block's GEMM runs at
+        # once on the current stream.  The arrival launch waits for the reset
+        # (so no flag of the previous call is seen), which follows the
+        # barrier: the NCCL kernel has finished before a kernel holding every
+        # SM waits on flags
         copy_streams, gemm_streams = pb.streams(1, 1)
         cs, gs = copy_streams[0], gemm_streams[0]
         fl = pb.flags.data_ptr()
