@@ -1,7 +1,8 @@
 """Sharded paths on >= 2 GPUs with NCCL (one process per GPU): the
 M-row-sharded GEMM with the B broadcast, rows x column panels with the
-all-gather or copy-engine pulls, the gather of C to one rank, and batch
-sharding give the same bits as the single-GPU call.
+all-gather or copy-engine pulls (each GEMM scheduling of the pulls), the
+gather of C to one rank, and batch sharding give the same bits as the
+single-GPU call.
 Skipped with fewer than two GPUs."""
 
 import os
@@ -52,11 +53,20 @@ def _worker(rank, world, port, out_dir):
             p0, p1 = ozd.column_panel(n, world, rank)
             want_n = oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4, torch.int8)[lo:hi]
             # collective all-gather, then copy-engine pulls (three calls: both
-            # buffer sets of the alternation, and the reuse of the first)
+            # buffer sets of the alternation, and the reuse of the first) with
+            # each GEMM scheduling of the p2p transport: the peer blocks in one
+            # arrival-flag launch (default), every block in it, a launch per block
             for transport in ("collective", "p2p", "p2p", "p2p"):
                 cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4,
                                               torch.int8, transport=transport)
                 ok1 = ok1 and torch.equal(cs, want_n)
+            default_mode = ozd.P2P_ONE_LAUNCH
+            for mode in ("all", None, "all"):
+                ozd.P2P_ONE_LAUNCH = mode
+                cs = ozd.ozaki_matmul_sharded(A[lo:hi].to(dev), Bn[:, p0:p1].to(dev), 4,
+                                              torch.int8, transport="p2p")
+                ok1 = ok1 and torch.equal(cs, want_n)
+            ozd.P2P_ONE_LAUNCH = default_mode
             # C gathered to rank 1: the whole product there, own rows elsewhere
             full_n = oz.ozaki_matmul(A.to(dev), Bn.to(dev), 4, torch.int8)
             for transport in ("collective", "p2p"):
